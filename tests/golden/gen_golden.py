@@ -1,0 +1,320 @@
+"""Record golden vectors from the reference implementation.
+
+Runs only where the reference checkout is present (it is read from
+``/root/reference``); the GPU machines and the test suite use the committed
+``.npz`` files instead. Regenerate with::
+
+    python tests/golden/gen_golden.py
+
+What is recorded (all from the reference's own code, unmodified):
+
+* ``mask_*.npz`` -- ``StructureAwareMaskBuilder._build_block_mask_from_chunks``
+  (methods/sabrecoder/sabrecoder_attention_triton.py:1455-1604) on seeded
+  synthetic chunk sets, plus the token-level inputs the reference derives
+  (``_map_tokens_to_chunks`` :807-858, signature/special lines mapped to
+  tokens :1557-1572), and ``compute_block_indices_from_mask`` (:1837-1859)
+  both raw and canonicalised (rows sorted).
+* ``mask_pyspecial.npz`` -- the Python special-line rules (:697-752) on a
+  synthetic Python-like file with a multi-token-per-line tokenizer.
+* ``builder_full.npz`` -- ``build_block_indices`` (:1606-1819) end to end with
+  the segmenter and reference analyser replaced by fixed chunk/edge lists
+  (tree-sitter is not installed), covering ``_append_uncovered_line_chunks``.
+* ``attn_*.npz`` -- ``_fwd_kernel_sabrecoder`` (:28-116) run by Triton's
+  interpreter in fp32 on bf16-representable inputs.
+* ``sparsity_utils.json`` -- utils/sparsity_utils.py values.
+
+The tree-sitter modules (pinned tree-sitter==0.20.4,
+tree-sitter-languages==1.10.2 in the reference's requirements.txt) are
+replaced by empty stand-ins so the module imports; nothing here parses code.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+import types
+
+os.environ["TRITON_INTERPRET"] = "1"
+REF = "/root/reference"
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+
+for _name in ("tree_sitter_languages", "tree_sitter"):
+    _m = types.ModuleType(_name)
+    _m.get_parser = lambda *a, **k: None
+    _m.Node = object
+    sys.modules[_name] = _m
+sys.path.insert(0, os.path.join(REF, "methods", "sabrecoder"))
+sys.path.insert(0, REF)
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+import sabrecoder_attention_triton as R  # noqa: E402
+from semantic_chunker import ChunkType, CodeChunk  # noqa: E402
+from utils import sparsity_utils as SU  # noqa: E402
+
+from sabrecoder_b200.spans import LineTokenizer, WordTokenizer, make_spans, spans_to_code  # noqa: E402
+
+_TYPE = {"import": ChunkType.IMPORT, "function": ChunkType.FUNCTION, "class": ChunkType.CLASS,
+         "statement": ChunkType.MODULE_CODE}
+_TYPE_CODE = {ChunkType.IMPORT: 0, ChunkType.FUNCTION: 1, ChunkType.CLASS: 2, ChunkType.METHOD: 3,
+              ChunkType.MODULE_CODE: 4, ChunkType.COMMENT: 5, ChunkType.DOCSTRING: 6}
+
+
+def chunks_from_spanset(ss):
+    out = []
+    for s in ss.spans:
+        sig = s.start + 1 if s.has_signature else None
+        out.append(CodeChunk(_TYPE[s.tag], 0, 0, "", name=f"s{s.start}", start_line=s.start + 1,
+                             end_line=s.end + 1, signature_start_line=sig, signature_end_line=sig))
+    return out
+
+
+def deps_to_arrays(deps):
+    src, dst = [], []
+    for s in sorted(deps):
+        for t in sorted(deps[s]):
+            src.append(int(s))
+            dst.append(int(t))
+    return np.asarray(src, np.int32), np.asarray(dst, np.int32)
+
+
+def chunk_arrays(chunks):
+    return dict(
+        chunk_type=np.asarray([_TYPE_CODE[c.chunk_type] for c in chunks], np.int32),
+        chunk_start_line=np.asarray([c.start_line for c in chunks], np.int32),
+        chunk_end_line=np.asarray([c.end_line for c in chunks], np.int32),
+        chunk_sig_start=np.asarray([c.signature_start_line or 0 for c in chunks], np.int32),
+        chunk_sig_end=np.asarray([c.signature_end_line or 0 for c in chunks], np.int32),
+        chunk_name=np.asarray([c.name or "" for c in chunks]),
+    )
+
+
+def record_mask(name, *, code, seq_len, chunks, deps, imports, language, tok, params):
+    mb = R.StructureAwareMaskBuilder(tok, **params)
+    bm = mb._build_block_mask_from_chunks(code=code, seq_len=seq_len, chunks=chunks,
+                                          chunk_deps=deps, import_chunks=imports, language=language)
+    t2c = np.asarray(mb._map_tokens_to_chunks(code, chunks, seq_len), np.int32)
+    vis = set()
+    for ch in chunks:
+        if ch.chunk_type in (ChunkType.FUNCTION, ChunkType.CLASS, ChunkType.METHOD):
+            if ch.signature_start_line and ch.signature_end_line:
+                vis.update(range(ch.signature_start_line, ch.signature_end_line + 1))
+    sp = mb._identify_special_lines(code, chunks, language=language)
+    for key in ("global_vars", "type_aliases", "class_attrs", "return_stmts"):
+        vis |= sp[key]
+    gtm = mb._map_lines_to_tokens(code, vis, seq_len).numpy().astype(np.uint8)
+    raw_idx, cnt = R.compute_block_indices_from_mask(bm.unsqueeze(0))
+    nb = bm.shape[0]
+    canon = np.full(raw_idx.shape, -1, np.int32)
+    for r in range(nb):
+        c = int(cnt[0, r])
+        canon[0, r, :c] = np.sort(raw_idx[0, r, :c].numpy())
+    dsrc, ddst = deps_to_arrays(deps)
+    np.savez_compressed(
+        os.path.join(HERE, f"mask_{name}.npz"),
+        code=np.asarray(code), seq_len=seq_len, language=np.asarray(language or ""),
+        tokenizer=np.asarray(tok.name_or_path), **{f"p_{k}": v for k, v in params.items()},
+        **chunk_arrays(chunks), dep_src=dsrc, dep_dst=ddst,
+        import_chunks=np.asarray(sorted(imports), np.int32),
+        token_to_chunk=t2c, global_token_mask=gtm, block_mask=bm.numpy().astype(np.uint8),
+        raw_indices=raw_idx.numpy(), block_counts=cnt.numpy(), indices_sorted=canon)
+    print(f"mask_{name}: L={seq_len} nb={nb} max_active={raw_idx.shape[-1]} "
+          f"density={float(bm.sum()) / (nb * (nb + 1) / 2):.3f}")
+
+
+def synthetic_python_file(seed, n_units=40):
+    """A Python-like file from fixed templates, and its chunk list."""
+    rng = np.random.default_rng(seed)
+    lines, chunks = [], []
+
+    def add(kind, body, name="", sig=True):
+        s = len(lines) + 1
+        lines.extend(body)
+        e = len(lines)
+        sl = s if sig else None
+        chunks.append(CodeChunk(kind, 0, 0, "\n".join(body), name=name, start_line=s, end_line=e,
+                                signature_start_line=sl, signature_end_line=sl))
+
+    add(ChunkType.IMPORT, ["import os", "from typing import List"], sig=False)
+    for u in range(n_units):
+        r = rng.random()
+        if r < 0.2:
+            lines.append(f"CONST_{u} = {u}")
+            lines.append(f"Alias{u} = List[int]")
+            lines.append("# note about constants")
+            lines.append("")
+        elif r < 0.5:
+            s = len(lines) + 1
+            body = [f"class K{u}:", "    def __init__(self, a):", "        self.a = a",
+                    "        self.b = a == 1", "        return None", f"    def m{u}(self):",
+                    "        return self.a"]
+            lines.extend(body)
+            chunks.append(CodeChunk(ChunkType.CLASS, 0, 0, "", name=f"K{u}", start_line=s,
+                                    end_line=s + 6, signature_start_line=s, signature_end_line=s))
+            chunks.append(CodeChunk(ChunkType.METHOD, 0, 0, "", name="__init__", start_line=s + 1,
+                                    end_line=s + 4, signature_start_line=s + 1, signature_end_line=s + 1))
+            chunks.append(CodeChunk(ChunkType.METHOD, 0, 0, "", name=f"m{u}", start_line=s + 5,
+                                    end_line=s + 6, signature_start_line=s + 5, signature_end_line=s + 5))
+        else:
+            n = int(rng.integers(2, 9))
+            body = [f"def f{u}(x, y):"] + ["    z = x + y" for _ in range(n)] + ["    if x >= y:",
+                                                                               "        return z", "    return x"]
+            add(ChunkType.FUNCTION, body, name=f"f{u}")
+    return "\n".join(lines), chunks
+
+
+class _Ref:
+    def __init__(self, s, t):
+        self.source_chunk_idx, self.target_chunk_idx = s, t
+
+
+def record_builder_full():
+    """build_block_indices end to end with a fixed segmenter/analyser."""
+    L = 1500
+    ss = make_spans(L, seed=77, max_len=120, p_function=0.4)
+    chunks = chunks_from_spanset(ss)
+    # Leave every 5th statement chunk out so _append_uncovered_line_chunks fills it.
+    seg_chunks = [c for i, c in enumerate(chunks) if not (c.chunk_type == ChunkType.MODULE_CODE and i % 5 == 0)]
+    edges = []
+    fun = [i for i, c in enumerate(seg_chunks) if c.chunk_type == ChunkType.FUNCTION]
+    for a, b in zip(fun[1::2], fun[::2]):
+        edges.append((a, b))
+
+    class Seg:
+        def __init__(self, tokenizer=None):
+            pass
+
+        def segment_code(self, code, language=None):
+            return list(seg_chunks)
+
+    class Ana:
+        def __init__(self, chunks, code, language=None):
+            pass
+
+        def analyze(self):
+            return [_Ref(a, b) for a, b in edges]
+
+    R.TreeSitterSegmenter, R.CrossReferenceAnalyzer = Seg, Ana
+    code = spans_to_code(ss)
+    params = dict(window_size=128, num_prefix_tokens=64, num_suffix_tokens=100, block_size=64,
+                  global_last_k_chunks=2, max_chunk_tokens=128)
+    mb = R.StructureAwareMaskBuilder(LineTokenizer(), **params)
+    bi, bc, bm = mb.build_block_indices(code, L, torch.device("cpu"), batch_size=2)
+    filled = mb._append_uncovered_line_chunks(code, seg_chunks)
+    nb = bm.shape[0]
+    canon = np.full(bi.shape, -1, np.int32)
+    for b in range(bi.shape[0]):
+        for r in range(nb):
+            c = int(bc[b, r])
+            canon[b, r, :c] = np.sort(bi[b, r, :c].numpy())
+    np.savez_compressed(
+        os.path.join(HERE, "builder_full.npz"), code=np.asarray(code), seq_len=L,
+        **{f"p_{k}": v for k, v in params.items()}, **chunk_arrays(seg_chunks),
+        **{f"filled_{k}": v for k, v in chunk_arrays(filled).items()},
+        edge_src=np.asarray([a for a, _ in edges], np.int32),
+        edge_dst=np.asarray([b for _, b in edges], np.int32),
+        block_mask=bm.numpy().astype(np.uint8), block_counts=bc.numpy(), indices_sorted=canon,
+        raw_indices=bi.numpy())
+    print(f"builder_full: nb={nb} chunks {len(seg_chunks)} -> {len(filled)} edges={len(edges)}")
+
+
+def record_attention(name, B, H, L, D, block, seed):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = [torch.randn(B, H, L, D, generator=g).to(torch.bfloat16).float() for _ in range(3)]
+    nb = (L + block - 1) // block
+    bm = (torch.rand(B, nb, nb, generator=g) < 0.5).int()
+    bm = bm | torch.eye(nb, dtype=torch.int32)
+    bm = torch.tril(bm)
+    bi, bc = R.compute_block_indices_from_mask(bm)
+    out = torch.empty_like(q)
+    R._fwd_kernel_sabrecoder[(nb, B * H)](
+        q, k, v, out, bi, bc, *q.stride(), *k.stride(), *v.stride(), *out.stride(), *bi.stride(),
+        *bc.stride(), B, H, L, max_active_blocks=bi.shape[2], BLOCK_M=block, BLOCK_N=block,
+        BLOCK_DMODEL=D)
+
+    def bits(x):
+        return x.to(torch.bfloat16).view(torch.int16).numpy()
+
+    np.savez_compressed(os.path.join(HERE, f"attn_{name}.npz"), q_bf16=bits(q), k_bf16=bits(k),
+                        v_bf16=bits(v), block_indices=bi.numpy(), block_counts=bc.numpy(),
+                        block_size=block, out=out.numpy())
+    print(f"attn_{name}: B={B} H={H} L={L} block={block} max_active={bi.shape[2]}")
+
+
+def record_sparsity_utils():
+    vals = {
+        "causal_total_blocks": [[m, n, SU.causal_total_blocks(m, n)] for m, n in
+                                [(0, 0), (1, 1), (5, 5), (7, 3), (3, 7), (256, 256), (192, 100)]],
+        "ceil_div": [[a, b, SU.ceil_div(a, b)] for a, b in [(0, 64), (1, 64), (64, 64), (65, 64), (16383, 64)]],
+    }
+    km = [0] * 1000
+    for i in (3, 70, 71, 500, 999):
+        km[i] = 1
+    vals["window_plus_keys"] = [
+        [L, w, bs, list(SU.causal_active_blocks_window_plus_keys(L, w, key_token_mask=km[:L] if L == 1000 else None,
+                                                                   block_size=bs))]
+        for L, w, bs in [(1000, 0, 64), (1000, 64, 64), (1000, 192, 64), (1000, 100, 128), (4096, 192, 64),
+                         (0, 64, 64)]]
+    vals["attend_ratio_from_cap"] = [[L, c, SU.causal_attend_ratio_from_cap(L, c)] for L, c in
+                                     [(100, 10), (4096, 300.5), (0, 1), (10, 100)]]
+    with open(os.path.join(HERE, "sparsity_utils.json"), "w") as f:
+        json.dump(vals, f, indent=1)
+    print("sparsity_utils.json")
+
+
+def main():
+    base = dict(window_size=192, num_prefix_tokens=64, num_suffix_tokens=128, block_size=64,
+                global_last_k_chunks=0, max_chunk_tokens=128)
+    cases = [
+        # name, L, seed, params-override, tokenizer
+        ("c0_4096", 4096, 0, {}, "line"),
+        ("c1_12288", 12288, 1, {}, "line"),
+        ("c3_16384", 16384, 3, {}, "line"),
+        ("ragged_1000", 1000, 5, dict(window_size=64, num_prefix_tokens=4, num_suffix_tokens=300,
+                                      global_last_k_chunks=2, max_chunk_tokens=0), "line"),
+        ("tiny_40", 40, 6, dict(window_size=0, num_prefix_tokens=0, num_suffix_tokens=0,
+                                global_last_k_chunks=1, max_chunk_tokens=0), "line"),
+        ("blk128_3000", 3000, 7, dict(block_size=128, window_size=384, max_chunk_tokens=256,
+                                      num_suffix_tokens=5000, global_last_k_chunks=3), "line"),
+        ("blk128_16384", 16384, 4, dict(block_size=128, window_size=384, num_suffix_tokens=128), "line"),
+        ("mct256_2047", 2047, 8, dict(max_chunk_tokens=256, window_size=100, num_prefix_tokens=200), "line"),
+        ("words_900", 900, 9, dict(window_size=64, global_last_k_chunks=2), "word"),
+    ]
+    for name, L, seed, over, tk in cases:
+        ss = make_spans(L, seed)
+        code = spans_to_code(ss)
+        chunks = chunks_from_spanset(ss)
+        deps = {int(k): set(int(x) for x in v) for k, v in ss.deps.items()}
+        if name == "ragged_1000":
+            # out-of-range ids are skipped by the reference (:1530, :1537, :1551)
+            deps.setdefault(0, set()).update({len(chunks) + 5, -1})
+            deps[len(chunks) + 2] = {0}
+            imports = set(ss.import_chunks) | {len(chunks) + 1}
+        else:
+            imports = set(ss.import_chunks)
+        if tk == "word":
+            code = "\n".join(" ".join(f"w{j}" for j in range(1 + (i % 3))) for i in range(L))
+            L = 900  # tokens (lines have 1-3 words + one special token)
+        params = dict(base)
+        params.update(over)
+        record_mask(name, code=code, seq_len=L, chunks=chunks, deps=deps, imports=imports, language=None,
+                    tok=LineTokenizer() if tk == "line" else WordTokenizer(), params=params)
+    code, chunks = synthetic_python_file(11)
+    params = dict(base)
+    params.update(window_size=64, num_prefix_tokens=16, num_suffix_tokens=32, global_last_k_chunks=1)
+    L = 700
+    imports = {i for i, c in enumerate(chunks) if c.chunk_type == ChunkType.IMPORT}
+    record_mask("pyspecial", code=code, seq_len=L, chunks=chunks, deps={}, imports=imports, language="python",
+                tok=WordTokenizer(), params=dict(params, block_size=16, max_chunk_tokens=32))
+    record_builder_full()
+    record_attention("b64", B=2, H=1, L=200, D=128, block=64, seed=21)
+    record_attention("b128", B=1, H=1, L=300, D=128, block=128, seed=22)
+    record_sparsity_utils()
+
+
+if __name__ == "__main__":
+    main()
