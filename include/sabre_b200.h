@@ -1,0 +1,176 @@
+/*
+ * sabre_b200.h -- C ABI of libsabre_b200.so, the sm_100a (B200) kernels
+ * behind SabreCoder's structure-aware block-sparse attention path.
+ *
+ * Conventions for every entry point:
+ *  - Plain pointers and sizes; all tensors are device pointers unless stated
+ *    otherwise; the caller allocates every buffer (no entry point allocates
+ *    device memory).
+ *  - Strides are in ELEMENTS, int64, in the order given by each function.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *  - Work is stream-ordered; entry points validate arguments on the host and
+ *    return SABRE_OK (0) or a negative sabre_status_t WITHOUT launching on
+ *    error. `sabre_last_error()` gives a message for the calling thread.
+ *  - Kernels never trap. A bounded device-side wait that runs out records
+ *    SABRE_DEV_TIMEOUT in a device status word (see sabre_device_status).
+ *  - dtype: SABRE_BF16 or SABRE_F16 for Q/K/V/O; index lists are int32.
+ */
+#ifndef SABRE_B200_H_
+#define SABRE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  SABRE_OK = 0,
+  SABRE_ERR_INVALID_ARG = -1,  /* bad pointer, size or stride */
+  SABRE_ERR_UNSUPPORTED = -2,  /* shape this build does not handle (e.g. head_dim != 128) */
+  SABRE_ERR_ALIGNMENT = -3,    /* pointer or stride breaks the 16-byte TMA rule */
+  SABRE_ERR_CUDA = -4,         /* a CUDA runtime/driver call failed */
+  SABRE_ERR_WORKSPACE = -5     /* workspace missing or too small */
+} sabre_status_t;
+
+enum { SABRE_BF16 = 0, SABRE_F16 = 1 };
+
+/* Device status flags (sabre_device_status). */
+enum { SABRE_DEV_TIMEOUT = 1u, SABRE_DEV_BAD_SMEM_ALIGN = 2u };
+
+int sabre_version(void);
+const char* sabre_status_string(int status);
+const char* sabre_last_error(void);
+
+/* Read (and optionally clear) the device status word of the current device.
+ * Synchronises `stream`. */
+int sabre_device_status(unsigned int* flags_out, int clear, void* stream);
+
+/* ------------------------------------------------------------------------
+ * (1) Block-sparse prefill attention.
+ *
+ * Replaces the launch of `_fwd_kernel_sabrecoder`
+ * (methods/sabrecoder/sabrecoder_attention_triton.py:2039-2053; kernel
+ * :28-116) from StructureAwareSparseAttentionTriton.forward (:1935-2066).
+ *
+ * q, o      : [B, Hq, L, D] strides q_strides/o_strides = {b, h, l, d}
+ * k, v      : [B, Hkv, L, D] strides {b, h, l, d}; query head h reads kv head
+ *             h / (Hq / Hkv) (the reference wrapper's repeat_interleave,
+ *             sabrecoder_llama_triton.py:301-303, without the copy)
+ * block_indices : int32 [B, Hidx, nb, max_active], strides idx_strides =
+ *             {b, h, m, k}; h-stride 0 shares one list across heads (the
+ *             reference's layout (B, nb, max_active))
+ * block_counts  : int32 [B, Hidx, nb], strides cnt_strides = {b, h, m}
+ * nb = ceil(L / block_size); block_size must be a multiple of 64;
+ * head_dim must be 128; d-stride must be 1; other strides and base pointers
+ * must be 16-byte multiples; L <= 65536.
+ * Semantics: for each (b, h, query row r) softmax over keys n <= r inside
+ * the listed blocks i < min(count, max_active); entries outside
+ * [0, query block] contribute nothing (the reference's causal mask makes
+ * them all -inf); duplicate entries count once. softmax_scale <= 0 selects
+ * 1/sqrt(head_dim) (the reference's scale, :67).
+ * ---------------------------------------------------------------------- */
+int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, const int32_t* block_indices,
+                      const int32_t* block_counts, int batch, int heads_q, int heads_kv, int seq_len,
+                      int head_dim, int block_size, int max_active, const int64_t* q_strides,
+                      const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                      const int64_t* idx_strides, const int64_t* cnt_strides, float softmax_scale, int dtype,
+                      void* stream);
+
+/* ------------------------------------------------------------------------
+ * (2) Split-K block-sparse decode attention over a KV cache.
+ *
+ * No reference counterpart for the sparse case: the reference decodes with
+ * dense SDPA over the whole cache (sabrecoder_llama_triton.py:254-268,
+ * :305-308). This entry replaces that SDPA call.
+ *
+ * q, o      : [B, Hq, D], strides {b, h, d}
+ * k_cache, v_cache : [B, Hkv, Tmax, D], strides {b, h, t, d}
+ * block_indices : int32 [B, Hidx, max_active] strides {b, h, k} (h-stride 0
+ *             = shared), block_counts int32 [B, Hidx] strides {b, h}
+ * seq_lens  : int32 [B] device: keys t >= seq_lens[b] are masked
+ * workspace : >= sabre_decode_workspace_size(...) bytes of device memory
+ * ---------------------------------------------------------------------- */
+size_t sabre_decode_workspace_size(int batch, int heads_q, int heads_kv, int head_dim, int max_active);
+int sabre_decode_bsa(const void* q, const void* k_cache, const void* v_cache, void* o,
+                     const int32_t* block_indices, const int32_t* block_counts, const int32_t* seq_lens,
+                     int batch, int heads_q, int heads_kv, int max_seq, int head_dim, int block_size,
+                     int max_active, const int64_t* q_strides, const int64_t* k_strides,
+                     const int64_t* v_strides, const int64_t* o_strides, const int64_t* idx_strides,
+                     const int64_t* cnt_strides, float softmax_scale, int dtype, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * (3) Block-mask construction from token-level structure.
+ *
+ * Replaces `StructureAwareMaskBuilder._build_block_mask_from_chunks`
+ * (sabrecoder_attention_triton.py:1455-1604): rules R0 window (:1492-1500),
+ * R1 within-chunk (:1502-1525), R2 dependencies (:1527-1544), R3 global key
+ * columns (:1546-1600), then tril (:1603).
+ *
+ * token_to_chunk : int32 [L] chunk id per token, -1 = none
+ * global_token_mask : uint8 [L] or NULL; 1 = token on a signature/special line
+ * chunk_flags : uint8 [nchunks]; bit 0 = import chunk (global key columns)
+ * dep_ptr, dep_idx : CSR of chunk dependencies, src -> targets (int32
+ *             [nchunks+1], [dep_ptr[nchunks]]); out-of-range targets skipped
+ * mask_bits (out): uint32 [nb, nwords], nwords = ceil(nb/32), bit j of row i
+ *             = block (i, j) active
+ * mask_dense (out, optional): int32 [nb, nb] (the reference's block_mask_2d)
+ * workspace : >= sabre_block_mask_workspace_size(nchunks, nb) bytes
+ * ---------------------------------------------------------------------- */
+size_t sabre_block_mask_workspace_size(int nchunks, int num_blocks);
+int sabre_build_block_mask(const int32_t* token_to_chunk, const uint8_t* global_token_mask,
+                           const uint8_t* chunk_flags, int nchunks, const int32_t* dep_ptr,
+                           const int32_t* dep_idx, int seq_len, int block_size, int window_size,
+                           int num_prefix_tokens, int num_suffix_tokens, int max_chunk_tokens,
+                           int global_last_k_chunks, uint32_t* mask_bits, int32_t* mask_dense, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * (3b) Index lists from a block mask.
+ *
+ * Replaces `compute_block_indices_from_mask`
+ * (sabrecoder_attention_triton.py:1837-1859). Rows are emitted in ascending
+ * column order (the reference's unstable argsort leaves the order arbitrary;
+ * counts and per-row sets are identical), padded with -1 up to `cap`.
+ * max_active_out (device int32[1]) receives max(max(counts), 1).
+ *
+ * From bits:  mask_bits uint32 [rows, nwords] -> indices int32 [rows, cap],
+ *             counts int32 [rows]; rows = batch * heads * nb (any layout the
+ *             caller flattens).
+ * From dense: mask int32 [rows, ncols] with row stride `mask_row_stride`.
+ * ---------------------------------------------------------------------- */
+int sabre_indices_from_bits(const uint32_t* mask_bits, int rows, int ncols, int32_t* indices, int cap,
+                            int32_t* counts, int32_t* max_active_out, void* stream);
+int sabre_indices_from_dense(const int32_t* mask, int rows, int ncols, int64_t mask_row_stride,
+                             int32_t* indices, int cap, int32_t* counts, int32_t* max_active_out,
+                             void* stream);
+
+/* ------------------------------------------------------------------------
+ * (3c) Pooled q.k top-k extension (no reference counterpart; nearest
+ * analogue is the chunk-similarity top-k, sabrecoder_attention_triton.py:
+ * 581-682: mean-pool, score, per-source top-k).
+ *
+ * sabre_pool_blocks: x [B, H, L, D] strides {b,h,l,d} -> out fp32
+ *   [B, H, nb, D] (contiguous): per block, rows summed first to last in
+ *   fp32 then divided by the row count.
+ * sabre_topk_extend: for each (b, h, query block qb) take the base row
+ *   (base_bits [nb, nwords], shared by all heads), add the `topk` blocks
+ *   kb <= qb not already active with the largest score
+ *   sum_d qm[b,h,qb,d] * km[b,h/(Hq/Hkv),kb,d] (fp32, products rounded, added
+ *   in order d = 0..D-1), ties to the lower kb; write the merged rows as
+ *   ascending index lists int32 [B, Hq, nb, cap] + counts [B, Hq, nb] and
+ *   max_active_out. Optional out_bits uint32 [B, Hq, nb, nwords].
+ * ---------------------------------------------------------------------- */
+int sabre_pool_blocks(const void* x, int batch, int heads, int seq_len, int head_dim, int block_size,
+                      const int64_t* x_strides, int dtype, float* out, void* stream);
+int sabre_topk_extend(const float* q_pooled, const float* k_pooled, const uint32_t* base_bits, int batch,
+                      int heads_q, int heads_kv, int num_blocks, int head_dim, int topk, int32_t* indices,
+                      int cap, int32_t* counts, int32_t* max_active_out, uint32_t* out_bits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SABRE_B200_H_ */

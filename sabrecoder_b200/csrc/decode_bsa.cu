@@ -1,0 +1,353 @@
+// Split-K block-sparse decode attention over a KV cache (sm_100a).
+//
+// The reference decodes one token with dense SDPA over the whole cache
+// (methods/sabrecoder/sabrecoder_llama_triton.py:254-268, :305-308); this
+// kernel reads only the listed key blocks. It is HBM-bound: each CTA streams
+// the K and V rows of its share of one KV head's block list with 16-byte
+// coalesced loads (a warp covers 512 contiguous bytes per instruction: two
+// 256-byte rows), scores all query heads of the GQA group against each row,
+// and keeps an online softmax per (warp half, head). The CTA's partial
+// (max, sum, acc[D]) goes to the workspace; a second kernel merges the
+// splits in a fixed order, so results are deterministic.
+#include "common.cuh"
+
+namespace sabre {
+namespace decode {
+
+constexpr int kD = 128;
+constexpr int kThreads = 128;       // 4 warps
+constexpr int kRowsPerHalf = 4;     // rows per half-warp per step
+constexpr int kRowsPerStep = 4 * 2 * kRowsPerHalf;  // 32 rows per CTA step
+constexpr int kTargetCtas = 4 * 148;
+constexpr int kMaxSplits = 256;
+
+struct Params {
+  const void* q;
+  const void* kc;
+  const void* vc;
+  void* o;
+  const int32_t* idx;
+  const int32_t* cnt;
+  const int32_t* seq_lens;
+  float* part_acc;  // [B][Hq][splits][D]
+  float* part_ml;   // [B][Hq][splits][2]
+  long long q_sb, q_sh;
+  long long k_sb, k_sh, k_st;
+  long long v_sb, v_sh, v_st;
+  long long o_sb, o_sh;
+  long long idx_sb, idx_sh, idx_sk;
+  long long cnt_sb, cnt_sh;
+  int B, Hq, Hkv, Tmax, block, max_active, splits, bps;
+  float scale_log2;
+};
+
+static inline int choose_splits(int batch, int heads_kv, int max_active) {
+  long long groups = static_cast<long long>(batch) * heads_kv;
+  int s = static_cast<int>((kTargetCtas + groups - 1) / groups);
+  s = s < 1 ? 1 : s;
+  s = s > max_active ? max_active : s;
+  return s > kMaxSplits ? kMaxSplits : s;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8], bool bf16) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (bf16) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    } else {
+      const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      const float2 ff = __half22float2(h);
+      f[2 * i] = ff.x;
+      f[2 * i + 1] = ff.y;
+    }
+  }
+}
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kThreads) decode_split_kernel(const Params p) {
+  constexpr bool kBf16 = DT<T>::kBf16;
+  const int split = blockIdx.x;
+  const int hk = blockIdx.y;
+  const int b = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int half = lane >> 4;
+  const int c = lane & 15;  // 16-byte chunk of the 256-byte row
+  const int g = p.Hq / p.Hkv;
+  const unsigned full = 0xffffffffu;
+
+  __shared__ float sm_m[8][G];
+  __shared__ float sm_l[8][G];
+  __shared__ float sm_acc[8][G][kD];
+
+  // q chunk for each head of the group, pre-scaled into the log2 domain.
+  float qv[G][8];
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi) {
+    if (gi < g) {
+      const T* qp = static_cast<const T*>(p.q) + b * p.q_sb + (hk * g + gi) * p.q_sh + c * 8;
+      const uint4 u = *reinterpret_cast<const uint4*>(qp);
+      unpack8(u, qv[gi], kBf16);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qv[gi][e] *= p.scale_log2;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qv[gi][e] = 0.f;
+    }
+  }
+  float m[G], l[G], acc[G][8];
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi) {
+    m[gi] = -INFINITY;
+    l[gi] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[gi][e] = 0.f;
+  }
+
+  const int T_valid = min(p.seq_lens[b], p.Tmax);
+  int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];
+  cnt = min(cnt, p.max_active);
+  const int j0 = split * p.bps;
+  const int j1 = min(j0 + p.bps, cnt);
+  const int32_t* ip = p.idx + b * p.idx_sb + hk * p.idx_sh;
+  const T* kbase = static_cast<const T*>(p.kc) + b * p.k_sb + hk * p.k_sh + c * 8;
+  const T* vbase = static_cast<const T*>(p.vc) + b * p.v_sb + hk * p.v_sh + c * 8;
+
+  for (int jj = j0; jj < j1; ++jj) {
+    const int kb = ip[jj * p.idx_sk];
+    if (kb < 0) continue;
+    const long long t_blk = static_cast<long long>(kb) * p.block;
+    if (t_blk >= T_valid) continue;
+    for (int rb = 0; rb < p.block; rb += kRowsPerStep) {
+      uint4 kr[kRowsPerHalf], vr[kRowsPerHalf];
+      bool valid[kRowsPerHalf];
+#pragma unroll
+      for (int u = 0; u < kRowsPerHalf; ++u) {
+        const int row = rb + warp * (2 * kRowsPerHalf) + 2 * u + half;
+        const long long t = t_blk + row;
+        valid[u] = (row < p.block) && (t < T_valid);
+        if (valid[u]) {
+          kr[u] = __ldg(reinterpret_cast<const uint4*>(kbase + t * p.k_st));
+          vr[u] = __ldg(reinterpret_cast<const uint4*>(vbase + t * p.v_st));
+        } else {
+          kr[u] = make_uint4(0u, 0u, 0u, 0u);
+          vr[u] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      float s[kRowsPerHalf][G];
+#pragma unroll
+      for (int u = 0; u < kRowsPerHalf; ++u) {
+        float kf[8];
+        unpack8(kr[u], kf, kBf16);
+#pragma unroll
+        for (int gi = 0; gi < G; ++gi) {
+          float d = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) d = fmaf(qv[gi][e], kf[e], d);
+          d += __shfl_xor_sync(full, d, 8);
+          d += __shfl_xor_sync(full, d, 4);
+          d += __shfl_xor_sync(full, d, 2);
+          d += __shfl_xor_sync(full, d, 1);
+          s[u][gi] = valid[u] ? d : -INFINITY;
+        }
+      }
+#pragma unroll
+      for (int gi = 0; gi < G; ++gi) {
+        float mt = s[0][gi];
+#pragma unroll
+        for (int u = 1; u < kRowsPerHalf; ++u) mt = fmaxf(mt, s[u][gi]);
+        const float mn = fmaxf(m[gi], mt);
+        if (mn == -INFINITY) continue;
+        const float alpha = ex2(m[gi] - mn);
+        float pr[kRowsPerHalf];
+        float ps = 0.f;
+#pragma unroll
+        for (int u = 0; u < kRowsPerHalf; ++u) {
+          pr[u] = ex2(s[u][gi] - mn);
+          ps += pr[u];
+        }
+        l[gi] = l[gi] * alpha + ps;
+        m[gi] = mn;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[gi][e] *= alpha;
+#pragma unroll
+        for (int u = 0; u < kRowsPerHalf; ++u) {
+          float vf[8];
+          unpack8(vr[u], vf, kBf16);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[gi][e] = fmaf(pr[u], vf[e], acc[gi][e]);
+        }
+      }
+    }
+  }
+
+  // Merge the 8 (warp, half) partial states of the CTA.
+  const int grp = warp * 2 + half;
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi) {
+    if (c == 0) {
+      sm_m[grp][gi] = m[gi];
+      sm_l[grp][gi] = l[gi];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sm_acc[grp][gi][c * 8 + e] = acc[gi][e];
+  }
+  __syncthreads();
+  const int d = tid;  // kThreads == kD
+  for (int gi = 0; gi < g && gi < G; ++gi) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) M = fmaxf(M, sm_m[r][gi]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float w = ex2(sm_m[r][gi] - M);
+        L += w * sm_l[r][gi];
+        A += w * sm_acc[r][gi][d];
+      }
+    }
+    const long long slot = (static_cast<long long>(b) * p.Hq + (hk * g + gi)) * p.splits + split;
+    p.part_acc[slot * kD + d] = A;
+    if (d == 0) {
+      p.part_ml[slot * 2] = M;
+      p.part_ml[slot * 2 + 1] = L;
+    }
+  }
+}
+
+// One CTA per (b, query head): merge the splits in index order.
+template <typename T>
+__global__ void __launch_bounds__(kD) decode_combine_kernel(const Params p) {
+  const int bh = blockIdx.x;
+  const int b = bh / p.Hq;
+  const int h = bh - b * p.Hq;
+  const int d = threadIdx.x;
+  const long long base = static_cast<long long>(bh) * p.splits;
+  float M = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.part_ml[(base + s) * 2]);
+  float L = 0.f, A = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < p.splits; ++s) {
+      const float ms = p.part_ml[(base + s) * 2];
+      const float w = ex2(ms - M);
+      L += w * p.part_ml[(base + s) * 2 + 1];
+      A += w * p.part_acc[(base + s) * kD + d];
+    }
+  }
+  const float out = (L > 0.f) ? A / L : 0.f;
+  T* op = static_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh;
+  op[d] = DT<T>::from_f(out);
+}
+
+template <typename T>
+static void launch_decode(const Params& p, int g, cudaStream_t s) {
+  dim3 grid(p.splits, p.Hkv, p.B);
+  if (g <= 1)
+    decode_split_kernel<T, 1><<<grid, kThreads, 0, s>>>(p);
+  else if (g <= 2)
+    decode_split_kernel<T, 2><<<grid, kThreads, 0, s>>>(p);
+  else if (g <= 4)
+    decode_split_kernel<T, 4><<<grid, kThreads, 0, s>>>(p);
+  else
+    decode_split_kernel<T, 8><<<grid, kThreads, 0, s>>>(p);
+  decode_combine_kernel<T><<<p.B * p.Hq, kD, 0, s>>>(p);
+}
+
+}  // namespace decode
+}  // namespace sabre
+
+using namespace sabre;
+
+extern "C" {
+
+size_t sabre_decode_workspace_size(int batch, int heads_q, int heads_kv, int head_dim, int max_active) {
+  using namespace sabre::decode;
+  if (batch <= 0 || heads_q <= 0 || heads_kv <= 0 || head_dim <= 0 || max_active <= 0) return 0;
+  const size_t splits = static_cast<size_t>(choose_splits(batch, heads_kv, max_active));
+  return static_cast<size_t>(batch) * heads_q * splits * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
+}
+
+int sabre_decode_bsa(const void* q, const void* k_cache, const void* v_cache, void* o,
+                     const int32_t* block_indices, const int32_t* block_counts, const int32_t* seq_lens,
+                     int batch, int heads_q, int heads_kv, int max_seq, int head_dim, int block_size,
+                     int max_active, const int64_t* q_strides, const int64_t* k_strides,
+                     const int64_t* v_strides, const int64_t* o_strides, const int64_t* idx_strides,
+                     const int64_t* cnt_strides, float softmax_scale, int dtype, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  using namespace sabre::decode;
+  if (!q || !k_cache || !v_cache || !o || !block_indices || !block_counts || !seq_lens || !q_strides ||
+      !k_strides || !v_strides || !o_strides || !idx_strides || !cnt_strides)
+    return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_decode_bsa: null pointer argument");
+  if (batch <= 0 || heads_q <= 0 || heads_kv <= 0 || max_seq <= 0 || max_active <= 0 || block_size <= 0)
+    return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_decode_bsa: sizes must be positive");
+  if (heads_q % heads_kv != 0 || heads_q / heads_kv > 8)
+    return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_decode_bsa: heads_q/heads_kv must be an integer <= 8");
+  if (head_dim != kD) return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_decode_bsa: head_dim %d (only 128)", head_dim);
+  if (dtype != SABRE_BF16 && dtype != SABRE_F16)
+    return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_decode_bsa: dtype %d", dtype);
+  if (q_strides[2] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || o_strides[2] != 1)
+    return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_decode_bsa: head_dim stride must be 1");
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  if (!al16(q) || !al16(k_cache) || !al16(v_cache))
+    return sabre_fail(SABRE_ERR_ALIGNMENT, "sabre_decode_bsa: q/k_cache/v_cache must be 16-byte aligned");
+  const int64_t ss[6] = {q_strides[0], q_strides[1], k_strides[0], k_strides[1], k_strides[2], v_strides[2]};
+  for (int i = 0; i < 6; ++i)
+    if ((ss[i] * 2) % 16 != 0)
+      return sabre_fail(SABRE_ERR_ALIGNMENT, "sabre_decode_bsa: q/k/v strides must be 16-byte multiples");
+  if ((v_strides[0] * 2) % 16 != 0 || (v_strides[1] * 2) % 16 != 0)
+    return sabre_fail(SABRE_ERR_ALIGNMENT, "sabre_decode_bsa: v strides must be 16-byte multiples");
+  const size_t need = sabre_decode_workspace_size(batch, heads_q, heads_kv, head_dim, max_active);
+  if (!workspace || workspace_bytes < need)
+    return sabre_fail(SABRE_ERR_WORKSPACE, "sabre_decode_bsa: workspace %zu < %zu bytes", workspace_bytes, need);
+  Params p;
+  p.q = q;
+  p.kc = k_cache;
+  p.vc = v_cache;
+  p.o = o;
+  p.idx = block_indices;
+  p.cnt = block_counts;
+  p.seq_lens = seq_lens;
+  p.q_sb = q_strides[0];
+  p.q_sh = q_strides[1];
+  p.k_sb = k_strides[0];
+  p.k_sh = k_strides[1];
+  p.k_st = k_strides[2];
+  p.v_sb = v_strides[0];
+  p.v_sh = v_strides[1];
+  p.v_st = v_strides[2];
+  p.o_sb = o_strides[0];
+  p.o_sh = o_strides[1];
+  p.idx_sb = idx_strides[0];
+  p.idx_sh = idx_strides[1];
+  p.idx_sk = idx_strides[2];
+  p.cnt_sb = cnt_strides[0];
+  p.cnt_sh = cnt_strides[1];
+  p.B = batch;
+  p.Hq = heads_q;
+  p.Hkv = heads_kv;
+  p.Tmax = max_seq;
+  p.block = block_size;
+  p.max_active = max_active;
+  p.splits = choose_splits(batch, heads_kv, max_active);
+  p.bps = (max_active + p.splits - 1) / p.splits;
+  const size_t nslots = static_cast<size_t>(batch) * heads_q * p.splits;
+  p.part_acc = static_cast<float*>(workspace);
+  p.part_ml = p.part_acc + nslots * kD;
+  const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(head_dim));
+  p.scale_log2 = scale * 1.4426950408889634f;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int g = heads_q / heads_kv;
+  if (dtype == SABRE_BF16)
+    launch_decode<__nv_bfloat16>(p, g, s);
+  else
+    launch_decode<__half>(p, g, s);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return sabre_cuda_fail(e, "sabre_decode_bsa launch");
+  return SABRE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,242 @@
+"""Torch-facing calls into libsabre_b200.so.
+
+Every function launches the CUDA kernels through the C ABI on the current
+stream of the tensors' device. Buffers (outputs and workspaces) are
+allocated here through torch's caching allocator; the library itself never
+allocates. There is no CPU path: non-CUDA tensors raise.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from ._lib import SabreError, check, i64, lib
+
+DTYPE_CODE = {torch.bfloat16: 0, torch.float16: 1}
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need_cuda(**tensors) -> None:
+    for name, t in tensors.items():
+        if t is not None and not t.is_cuda:
+            raise SabreError(f"{name} must be a CUDA tensor (got {t.device}); this library has no CPU path")
+
+
+def _i32(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype != torch.int32:
+        raise SabreError(f"{name} must be int32 (got {t.dtype})")
+    return t
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+# ---------------------------------------------------------------------------
+# (1) prefill
+# ---------------------------------------------------------------------------
+
+def prefill_bsa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_indices: torch.Tensor,
+                block_counts: torch.Tensor, block_size: int, softmax_scale: Optional[float] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Block-sparse causal attention.
+
+    q: ``[B, Hq, L, D]``; k, v: ``[B, Hkv, L, D]`` (any strides with unit
+    head-dim stride, 16-byte aligned); block_indices ``[B, nb, max]`` (shared
+    by heads, the reference layout) or ``[B, Hq, nb, max]``; block_counts
+    ``[B, nb]`` or ``[B, Hq, nb]``. Returns ``[B, Hq, L, D]`` in q's dtype."""
+    _need_cuda(q=q, k=k, v=v, block_indices=block_indices, block_counts=block_counts)
+    if q.dtype not in DTYPE_CODE or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise SabreError(f"q/k/v must share dtype bf16 or f16 (got {q.dtype}, {k.dtype}, {v.dtype})")
+    B, Hq, L, D = q.shape
+    Hkv = k.shape[1]
+    if k.shape != (B, Hkv, L, D) or v.shape != k.shape:
+        raise SabreError(f"k/v shape {tuple(k.shape)}/{tuple(v.shape)} does not match q {tuple(q.shape)}")
+    bi = _i32(block_indices, "block_indices")
+    bc = _i32(block_counts, "block_counts")
+    if bi.dim() == 3:
+        idx_strides = (bi.stride(0), 0, bi.stride(1), bi.stride(2))
+        cnt_strides = (bc.stride(0), 0, bc.stride(1))
+    elif bi.dim() == 4:
+        if bi.shape[1] not in (1, Hq):
+            raise SabreError(f"block_indices head dim {bi.shape[1]} must be 1 or {Hq}")
+        idx_strides = (bi.stride(0), bi.stride(1) if bi.shape[1] > 1 else 0, bi.stride(2), bi.stride(3))
+        cnt_strides = (bc.stride(0), bc.stride(1) if bc.shape[1] > 1 else 0, bc.stride(2))
+    else:
+        raise SabreError(f"block_indices must be 3-D or 4-D (got {tuple(bi.shape)})")
+    nb = (L + block_size - 1) // block_size
+    if bi.shape[0] != B or bi.shape[-2] != nb or bc.shape[-1] != nb:
+        raise SabreError(f"index lists {tuple(bi.shape)} / counts {tuple(bc.shape)} do not match B={B}, nb={nb}")
+    if out is None:
+        out = torch.empty_like(q)
+    st = lib().sabre_prefill_bsa(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), bi.data_ptr(), bc.data_ptr(), B, Hq, Hkv, L, D,
+        int(block_size), int(bi.shape[-1]), i64(q.stride()), i64(k.stride()), i64(v.stride()), i64(out.stride()),
+        i64(idx_strides), i64(cnt_strides), float(softmax_scale or 0.0), DTYPE_CODE[q.dtype], _stream(q))
+    check(st, "sabre_prefill_bsa")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# (2) decode
+# ---------------------------------------------------------------------------
+
+def decode_workspace_bytes(batch: int, heads_q: int, heads_kv: int, head_dim: int, max_active: int) -> int:
+    return int(lib().sabre_decode_workspace_size(batch, heads_q, heads_kv, head_dim, max_active))
+
+
+def decode_bsa(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_indices: torch.Tensor,
+               block_counts: torch.Tensor, seq_lens: torch.Tensor, block_size: int,
+               softmax_scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+               workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One query row per sequence over the KV cache.
+
+    q: ``[B, Hq, D]``; k_cache, v_cache: ``[B, Hkv, Tmax, D]``;
+    block_indices ``[B, max]`` (shared by heads) or ``[B, Hkv, max]``;
+    block_counts ``[B]`` or ``[B, Hkv]``; seq_lens int32 ``[B]`` (device)."""
+    _need_cuda(q=q, k_cache=k_cache, v_cache=v_cache, block_indices=block_indices, block_counts=block_counts,
+               seq_lens=seq_lens)
+    if q.dtype not in DTYPE_CODE or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise SabreError("q/k_cache/v_cache must share dtype bf16 or f16")
+    B, Hq, D = q.shape
+    Hkv, Tmax = k_cache.shape[1], k_cache.shape[2]
+    bi = _i32(block_indices, "block_indices")
+    bc = _i32(block_counts, "block_counts")
+    _i32(seq_lens, "seq_lens")
+    if bi.dim() == 2:
+        idx_strides = (bi.stride(0), 0, bi.stride(1))
+        cnt_strides = (bc.stride(0), 0)
+    else:
+        idx_strides = (bi.stride(0), bi.stride(1) if bi.shape[1] > 1 else 0, bi.stride(2))
+        cnt_strides = (bc.stride(0), bc.stride(1) if bc.shape[1] > 1 else 0)
+    max_active = int(bi.shape[-1])
+    need = decode_workspace_bytes(B, Hq, Hkv, D, max_active)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+    if out is None:
+        out = torch.empty_like(q)
+    st = lib().sabre_decode_bsa(
+        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), bi.data_ptr(), bc.data_ptr(),
+        seq_lens.data_ptr(), B, Hq, Hkv, Tmax, D, int(block_size), max_active, i64(q.stride()),
+        i64(k_cache.stride()), i64(v_cache.stride()), i64(out.stride()), i64(idx_strides), i64(cnt_strides),
+        float(softmax_scale or 0.0), DTYPE_CODE[q.dtype], workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), _stream(q))
+    check(st, "sabre_decode_bsa")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# (3) mask + index lists
+# ---------------------------------------------------------------------------
+
+def build_block_mask(token_to_chunk: torch.Tensor, chunk_flags: torch.Tensor, dep_ptr: torch.Tensor,
+                     dep_idx: torch.Tensor, global_token_mask: Optional[torch.Tensor], *, seq_len: int,
+                     block_size: int, window_size: int, num_prefix_tokens: int, num_suffix_tokens: int,
+                     max_chunk_tokens: int, global_last_k_chunks: int,
+                     dense: bool = True) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Block mask from token-level structure. Returns ``(bits, dense)``:
+    bits int32 ``[nb, ceil(nb/32)]`` (uint32 words), dense int32 ``[nb, nb]``."""
+    _need_cuda(token_to_chunk=token_to_chunk, chunk_flags=chunk_flags, dep_ptr=dep_ptr, dep_idx=dep_idx,
+               global_token_mask=global_token_mask)
+    dev = token_to_chunk.device
+    nchunks = int(chunk_flags.numel())
+    nb = (seq_len + block_size - 1) // block_size
+    nwords = (nb + 31) // 32
+    bits = torch.empty(nb, nwords, dtype=torch.int32, device=dev)
+    dm = torch.empty(nb, nb, dtype=torch.int32, device=dev) if dense else None
+    ws_bytes = int(lib().sabre_block_mask_workspace_size(nchunks, nb))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    if global_token_mask is not None and global_token_mask.dtype != torch.uint8:
+        global_token_mask = global_token_mask.to(torch.uint8)
+    st = lib().sabre_build_block_mask(
+        _i32(token_to_chunk, "token_to_chunk").data_ptr(), _ptr(global_token_mask),
+        chunk_flags.data_ptr() if nchunks else None, nchunks, _i32(dep_ptr, "dep_ptr").data_ptr(),
+        _i32(dep_idx, "dep_idx").data_ptr() if dep_idx.numel() else None, int(seq_len), int(block_size),
+        int(window_size), int(num_prefix_tokens), int(num_suffix_tokens), int(max_chunk_tokens),
+        int(global_last_k_chunks), bits.data_ptr(), _ptr(dm), ws.data_ptr(), ws.numel(), _stream(bits))
+    check(st, "sabre_build_block_mask")
+    return bits, dm
+
+
+def indices_from_bits(bits: torch.Tensor, ncols: int, cap: Optional[int] = None):
+    """Ascending index lists from row bitsets ``[..., nwords]``. Returns
+    ``(indices [..., cap], counts [...], max_active device int32[1])``."""
+    _need_cuda(bits=bits)
+    lead = bits.shape[:-1]
+    rows = int(math.prod(lead)) if lead else 1
+    cap = int(ncols if cap is None else cap)
+    b = bits.reshape(rows, bits.shape[-1]).contiguous()
+    idx = torch.empty(rows, cap, dtype=torch.int32, device=bits.device)
+    cnt = torch.empty(rows, dtype=torch.int32, device=bits.device)
+    mx = torch.empty(1, dtype=torch.int32, device=bits.device)
+    check(lib().sabre_indices_from_bits(b.data_ptr(), rows, int(ncols), idx.data_ptr(), cap, cnt.data_ptr(),
+                                        mx.data_ptr(), _stream(bits)), "sabre_indices_from_bits")
+    return idx.reshape(*lead, cap), cnt.reshape(lead), mx
+
+
+def indices_from_dense(mask: torch.Tensor, cap: Optional[int] = None):
+    """Ascending index lists from a dense mask ``[..., nb, ncols]`` (nonzero =
+    active). Returns ``(indices [..., nb, cap], counts [..., nb], max_active)``."""
+    _need_cuda(mask=mask)
+    m = mask if mask.dtype == torch.int32 else mask.to(torch.int32)
+    lead = m.shape[:-1]
+    ncols = int(m.shape[-1])
+    rows = int(math.prod(lead))
+    m2 = m.reshape(rows, ncols)
+    if m2.stride(-1) != 1:
+        m2 = m2.contiguous()
+    cap = int(ncols if cap is None else cap)
+    idx = torch.empty(rows, cap, dtype=torch.int32, device=m.device)
+    cnt = torch.empty(rows, dtype=torch.int32, device=m.device)
+    mx = torch.empty(1, dtype=torch.int32, device=m.device)
+    check(lib().sabre_indices_from_dense(m2.data_ptr(), rows, ncols, m2.stride(0), idx.data_ptr(), cap,
+                                         cnt.data_ptr(), mx.data_ptr(), _stream(m)), "sabre_indices_from_dense")
+    return idx.reshape(*lead, cap), cnt.reshape(lead), mx
+
+
+def pool_blocks(x: torch.Tensor, block_size: int) -> torch.Tensor:
+    """Per-block mean of ``x [B, H, L, D]`` -> fp32 ``[B, H, nb, D]`` (rows
+    summed first to last in fp32, then divided by the row count)."""
+    _need_cuda(x=x)
+    B, H, L, D = x.shape
+    nb = (L + block_size - 1) // block_size
+    out = torch.empty(B, H, nb, D, dtype=torch.float32, device=x.device)
+    check(lib().sabre_pool_blocks(x.data_ptr(), B, H, L, D, int(block_size), i64(x.stride()), DTYPE_CODE[x.dtype],
+                                  out.data_ptr(), _stream(x)), "sabre_pool_blocks")
+    return out
+
+
+def topk_extend(q_pooled: torch.Tensor, k_pooled: torch.Tensor, base_bits: torch.Tensor, topk: int,
+                cap: Optional[int] = None, want_bits: bool = False):
+    """Per-(b, head) lists = base rows plus the top-k pooled-score blocks.
+    Returns ``(indices [B, Hq, nb, cap], counts [B, Hq, nb], max_active, bits|None)``."""
+    _need_cuda(q_pooled=q_pooled, k_pooled=k_pooled, base_bits=base_bits)
+    B, Hq, nb, D = q_pooled.shape
+    Hkv = k_pooled.shape[1]
+    qp = q_pooled.contiguous()
+    kp = k_pooled.contiguous()
+    bb = base_bits.contiguous()
+    cap = int(nb if cap is None else cap)
+    idx = torch.empty(B, Hq, nb, cap, dtype=torch.int32, device=qp.device)
+    cnt = torch.empty(B, Hq, nb, dtype=torch.int32, device=qp.device)
+    mx = torch.empty(1, dtype=torch.int32, device=qp.device)
+    ob = torch.empty(B, Hq, nb, bb.shape[-1], dtype=torch.int32, device=qp.device) if want_bits else None
+    check(lib().sabre_topk_extend(qp.data_ptr(), kp.data_ptr(), bb.data_ptr(), B, Hq, Hkv, nb, D, int(topk),
+                                  idx.data_ptr(), cap, cnt.data_ptr(), mx.data_ptr(), _ptr(ob), _stream(qp)),
+          "sabre_topk_extend")
+    return idx, cnt, mx, ob
+
+
+def device_status(clear: bool = True, stream: Optional[int] = None) -> int:
+    import ctypes
+    v = ctypes.c_uint(0)
+    s = stream if stream is not None else (torch.cuda.current_stream().cuda_stream if torch.cuda.is_available()
+                                           else None)
+    check(lib().sabre_device_status(ctypes.byref(v), 1 if clear else 0, s), "sabre_device_status")
+    return int(v.value)

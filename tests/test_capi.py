@@ -1,0 +1,74 @@
+"""The C-ABI library loads and exports every entry point include/sabre_b200.h
+declares; host-side validation rejects bad arguments without launching."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from sabrecoder_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    src = open(os.path.join(ROOT, "include", "sabre_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(sabre_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_the_bound_functions():
+    assert set(header_functions()) == set(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    for name in header_functions():
+        assert hasattr(L, name), name
+
+
+def test_status_strings_and_version():
+    L = _lib.lib()
+    assert L.sabre_version() >= 100
+    assert L.sabre_status_string(0) == b"ok"
+    assert b"workspace" in L.sabre_status_string(-5)
+
+
+def test_prefill_rejects_bad_arguments_before_launch():
+    L = _lib.lib()
+    st = _lib.i64([1, 1, 1, 1])
+    r = L.sabre_prefill_bsa(None, None, None, None, None, None, 1, 1, 1, 64, 128, 64, 1, st, st, st, st, st, st,
+                            0.0, 0, None)
+    assert r == -1 and b"null" in L.sabre_last_error()
+    fake = 16
+    r = L.sabre_prefill_bsa(fake, fake, fake, fake, fake, fake, 1, 1, 1, 64, 96, 64, 1, st, st, st, st, st, st,
+                            0.0, 0, None)
+    assert r == -2 and b"head_dim" in L.sabre_last_error()
+    r = L.sabre_prefill_bsa(fake, fake, fake, fake, fake, fake, 1, 1, 1, 64, 128, 32, 1, st, st, st, st, st, st,
+                            0.0, 0, None)
+    assert r == -2 and b"block_size" in L.sabre_last_error()
+    r = L.sabre_prefill_bsa(fake, fake, fake, fake, fake, fake, 1, 3, 2, 64, 128, 64, 1, st, st, st, st, st, st,
+                            0.0, 0, None)
+    assert r == -1 and b"multiple" in L.sabre_last_error()
+
+
+def test_decode_and_mask_reject_bad_arguments():
+    L = _lib.lib()
+    st = _lib.i64([1, 1, 1, 1])
+    r = L.sabre_decode_bsa(16, 16, 16, 16, 16, 16, 16, 1, 9, 1, 64, 128, 64, 1, st, st, st, st, st, st, 0.0, 0,
+                           None, 0, None)
+    assert r == -2
+    assert L.sabre_decode_workspace_size(1, 4, 4, 128, 10) > 0
+    r = L.sabre_build_block_mask(16, None, 16, 1, 16, None, 1000, 64, 64, 0, 0, 100, 0, 16, None, 16, 8, None)
+    assert r == -1 and b"multiple of block_size" in L.sabre_last_error()
+    r = L.sabre_build_block_mask(16, None, 16, 1, 16, None, 1000, 64, 64, 0, 0, 128, 0, 16, None, 16, 4, None)
+    assert r == -5
+
+
+def test_kernel_calls_fail_loudly_without_cuda_tensors():
+    import torch
+    from sabrecoder_b200 import kernels
+    q = torch.zeros(1, 1, 64, 128, dtype=torch.bfloat16)
+    with pytest.raises(_lib.SabreError, match="CUDA tensor"):
+        kernels.prefill_bsa(q, q, q, torch.zeros(1, 1, 1, dtype=torch.int32), torch.ones(1, 1, dtype=torch.int32), 64)

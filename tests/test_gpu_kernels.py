@@ -1,0 +1,240 @@
+"""GPU parity of the CUDA kernels against the oracle and the reference's
+recorded outputs. Tolerances (bf16): max-abs 2e-2, mean-abs 2e-3 for
+attention; bit-exact for masks, counts and index lists."""
+
+import numpy as np
+import pytest
+import torch
+
+import _golden as G
+from oracle import attention_oracle as AO
+from oracle import mask_oracle as MO
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MEAN_ABS = 2e-3
+
+
+@pytest.fixture(scope="module")
+def K():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from sabrecoder_b200 import kernels
+    kernels.device_status(clear=True)
+    return kernels
+
+
+def _close(out, ref, max_abs=MAX_ABS, mean_abs=MEAN_ABS):
+    d = (out.float().cpu() - ref.float().cpu()).abs()
+    assert d.max().item() <= max_abs, f"max-abs {d.max().item():.3e}"
+    assert d.mean().item() <= mean_abs, f"mean-abs {d.mean().item():.3e}"
+
+
+def _random_lists(B, nb, gen, density=0.3, heads=None):
+    shape = (B, nb, nb) if heads is None else (B, heads, nb, nb)
+    m = torch.rand(shape, generator=gen) < density
+    m = m | torch.eye(nb, dtype=torch.bool)
+    m = m.tril()
+    idx, cnt = MO.block_indices_from_mask(m.numpy())
+    return torch.from_numpy(idx), torch.from_numpy(cnt)
+
+
+@pytest.mark.parametrize("case", ["attn_b64.npz", "attn_b128.npz"])
+def test_prefill_matches_reference_kernel_output(K, case):
+    g = G.load(case)
+    q, k, v = (G.bf16_bits_to_f32(g[n]).to(torch.bfloat16).cuda() for n in ("q_bf16", "k_bf16", "v_bf16"))
+    bi = torch.from_numpy(g["block_indices"]).cuda()
+    bc = torch.from_numpy(g["block_counts"]).cuda()
+    out = K.prefill_bsa(q, k, v, bi, bc, int(g["block_size"]))
+    torch.cuda.synchronize()
+    _close(out, torch.from_numpy(g["out"]))
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,L,block,dtype,per_head,layout", [
+    (1, 2, 2, 1000, 64, torch.bfloat16, False, "bhld"),
+    (2, 4, 2, 512, 64, torch.bfloat16, False, "blhd"),
+    (1, 4, 4, 700, 64, torch.bfloat16, True, "blhd"),
+    (1, 2, 1, 900, 128, torch.bfloat16, False, "blhd"),
+    (1, 2, 2, 640, 64, torch.float16, False, "bhld"),
+    (1, 7, 1, 384, 128, torch.bfloat16, True, "blhd"),
+    (1, 1, 1, 65, 64, torch.bfloat16, False, "bhld"),
+    (1, 1, 1, 40, 64, torch.bfloat16, False, "bhld"),
+])
+def test_prefill_vs_oracle(K, B, Hq, Hkv, L, block, dtype, per_head, layout):
+    gen = torch.Generator().manual_seed(L + Hq + block)
+    D = 128
+
+    def mk(H):
+        if layout == "blhd":
+            return torch.randn(B, L, H, D, generator=gen).to(dtype).transpose(1, 2)
+        return torch.randn(B, H, L, D, generator=gen).to(dtype)
+
+    q, k, v = mk(Hq), mk(Hkv), mk(Hkv)
+    nb = (L + block - 1) // block
+    bi, bc = _random_lists(B, nb, gen, heads=Hq if per_head else None)
+    out = K.prefill_bsa(q.cuda(), k.cuda(), v.cuda(), bi.cuda(), bc.cuda(), block)
+    torch.cuda.synchronize()
+    ref = AO.sparse_prefill_fp32(q, k, v, bi, bc, block)
+    _close(out, ref)
+
+
+def test_prefill_ignores_invalid_entries(K):
+    """Entries beyond the count, negative, past the query block, or repeated
+    contribute nothing extra (the reference's causal mask drops the ones past
+    the query block; valid lists never hold the others)."""
+    gen = torch.Generator().manual_seed(3)
+    B, H, L, D, block = 1, 2, 512, 128, 64
+    q, k, v = (torch.randn(B, H, L, D, generator=gen).to(torch.bfloat16) for _ in range(3))
+    nb = L // block
+    bi, bc = _random_lists(B, nb, gen)
+    ref = AO.sparse_prefill_fp32(q, k, v, bi, bc, block)
+    cap = bi.shape[-1] + 3
+    junk = torch.full((B, nb, cap), -1, dtype=torch.int32)
+    for r in range(nb):
+        c = int(bc[0, r])
+        row = bi[0, r, :c].tolist()
+        extra = [-5, nb + 3, min(r + 1, nb - 1) if r + 1 < nb else r] + row[:1]
+        junk[0, r, : c + len(extra)] = torch.tensor((row + extra)[: cap], dtype=torch.int32)
+        bc[0, r] = min(c + len(extra), cap)
+    out = K.prefill_bsa(q.cuda(), k.cuda(), v.cuda(), junk.cuda(), bc.cuda(), block)
+    torch.cuda.synchronize()
+    _close(out, ref)
+
+
+def test_prefill_config0_shape(K):
+    """B=1, H=16, L=4096, D=128, block 64 with a structure mask + top-8."""
+    gen = torch.Generator().manual_seed(0)
+    B, H, L, D, block = 1, 16, 4096, 128, 64
+    q, k, v = (torch.randn(B, H, L, D, generator=gen).to(torch.bfloat16) for _ in range(3))
+    g = G.load("mask_c0_4096.npz")
+    base = g["block_mask"].astype(bool)
+    qm = MO.pooled_block_means(q.float().numpy(), L, block)
+    km = MO.pooled_block_means(k.float().numpy(), L, block)
+    ext = MO.topk_extend_mask(base, MO.pooled_scores(qm, km), 8)
+    idx, cnt = MO.block_indices_from_mask(ext)
+    bi, bc = torch.from_numpy(idx), torch.from_numpy(cnt)
+    out = K.prefill_bsa(q.cuda(), k.cuda(), v.cuda(), bi.cuda(), bc.cuda(), block)
+    torch.cuda.synchronize()
+    ref = AO.sparse_prefill_fp32(q, k, v, bi, bc, block)
+    _close(out, ref)
+    assert K.device_status(clear=True) == 0
+
+
+def _kernel_mask(K, g):
+    p = G.params(g)
+    L = int(g["seq_len"])
+    nchunks = g["chunk_type"].shape[0]
+    flags = np.zeros(max(nchunks, 1), np.uint8)[:nchunks]
+    for c in g["import_chunks"].tolist():
+        if 0 <= c < nchunks:
+            flags[c] |= 1
+    deps = G.deps(g)
+    ptr = np.zeros(nchunks + 1, np.int32)
+    flat = []
+    for c in range(nchunks):
+        tg = sorted(deps.get(c, ()))
+        flat.extend(tg)
+        ptr[c + 1] = len(flat)
+    dev = "cuda"
+    bits, dense = K.build_block_mask(
+        torch.from_numpy(g["token_to_chunk"].astype(np.int32)).to(dev), torch.from_numpy(flags).to(dev),
+        torch.from_numpy(ptr).to(dev), torch.tensor(flat, dtype=torch.int32, device=dev),
+        torch.from_numpy(g["global_token_mask"].astype(np.uint8)).to(dev), seq_len=L, **p)
+    return bits, dense
+
+
+@pytest.mark.parametrize("case", G.mask_cases())
+def test_block_mask_kernel_bit_exact(K, case):
+    g = G.load(case)
+    bits, dense = _kernel_mask(K, g)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(dense.cpu().numpy(), g["block_mask"])
+    nb = dense.shape[0]
+    idx, cnt, mx = K.indices_from_bits(bits, nb)
+    torch.cuda.synchronize()
+    ma = int(mx.item())
+    assert ma == g["indices_sorted"].shape[-1]
+    np.testing.assert_array_equal(cnt.cpu().numpy(), g["block_counts"][0])
+    np.testing.assert_array_equal(idx[:, :ma].cpu().numpy(), g["indices_sorted"][0])
+    idx2, cnt2, mx2 = K.indices_from_dense(dense.unsqueeze(0))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(idx2[..., :ma].cpu().numpy(), g["indices_sorted"])
+    assert int(mx2.item()) == ma
+
+
+def test_indices_from_dense_random(K):
+    gen = torch.Generator().manual_seed(5)
+    for nb in (1, 31, 32, 33, 200, 1100):
+        m = (torch.rand(3, nb, nb, generator=gen) < 0.2).int()
+        if nb == 33:
+            m.zero_()
+        idx, cnt, mx = K.indices_from_dense(m.cuda())
+        torch.cuda.synchronize()
+        ri, rc = MO.block_indices_from_mask(m.numpy())
+        ma = int(mx.item())
+        assert ma == ri.shape[-1]
+        np.testing.assert_array_equal(cnt.cpu().numpy(), rc)
+        np.testing.assert_array_equal(idx[..., :ma].cpu().numpy(), ri)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,L,block,topk", [(1, 4, 4, 1000, 64, 8), (1, 4, 2, 640, 64, 3),
+                                                    (2, 2, 2, 2000, 128, 8)])
+def test_pooled_topk_bit_exact(K, B, Hq, Hkv, L, block, topk):
+    gen = torch.Generator().manual_seed(L)
+    D = 128
+    q = torch.randn(B, L, Hq, D, generator=gen).to(torch.bfloat16).transpose(1, 2)
+    k = torch.randn(B, L, Hkv, D, generator=gen).to(torch.bfloat16).transpose(1, 2)
+    nb = (L + block - 1) // block
+    base = np.tril(np.random.default_rng(L).random((nb, nb)) < 0.15) | np.eye(nb, dtype=bool)
+    qm = K.pool_blocks(q.cuda(), block)
+    km = K.pool_blocks(k.cuda(), block)
+    torch.cuda.synchronize()
+    qm_ref = MO.pooled_block_means(q.float().numpy(), L, block)
+    km_ref = MO.pooled_block_means(k.float().numpy(), L, block)
+    np.testing.assert_array_equal(qm.cpu().numpy(), qm_ref)
+    np.testing.assert_array_equal(km.cpu().numpy(), km_ref)
+    nwords = (nb + 31) // 32
+    bits = np.zeros((nb, nwords), np.uint32)
+    for i in range(nb):
+        for j in np.nonzero(base[i])[0]:
+            bits[i, j // 32] |= np.uint32(1) << np.uint32(j % 32)
+    bits_t = torch.from_numpy(bits.view(np.int32)).cuda()
+    idx, cnt, mx, _ = K.topk_extend(qm, km, bits_t, topk)
+    torch.cuda.synchronize()
+    g = Hq // Hkv
+    sc = MO.pooled_scores(qm_ref, np.repeat(km_ref, g, axis=1))
+    ext = MO.topk_extend_mask(base, sc, topk)
+    ri, rc = MO.block_indices_from_mask(ext)
+    ma = int(mx.item())
+    assert ma == ri.shape[-1]
+    np.testing.assert_array_equal(cnt.cpu().numpy(), rc)
+    np.testing.assert_array_equal(idx[..., :ma].cpu().numpy(), ri)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Tmax,block,shared", [(1, 4, 4, 3000, 64, True), (2, 7, 1, 2048, 128, False),
+                                                         (3, 8, 2, 1500, 64, False), (1, 2, 2, 64, 64, True)])
+def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
+    gen = torch.Generator().manual_seed(Tmax + Hq)
+    D = 128
+    q = torch.randn(B, Hq, D, generator=gen).to(torch.bfloat16)
+    kc = torch.randn(B, Hkv, Tmax, D, generator=gen).to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, Tmax, D, generator=gen).to(torch.bfloat16)
+    seq = torch.randint(1, Tmax + 1, (B,), generator=gen).to(torch.int32)
+    nbk = (Tmax + block - 1) // block
+    H = 1 if shared else Hkv
+    m = torch.rand(B, H, nbk, generator=gen) < 0.4
+    for b in range(B):
+        m[b, :, (int(seq[b]) - 1) // block] = True
+    idx, cnt = MO.block_indices_from_mask(m.numpy())
+    bi, bc = torch.from_numpy(idx), torch.from_numpy(cnt)
+    if shared:
+        bi, bc = bi[:, 0], bc[:, 0]
+    out = K.decode_bsa(q.cuda(), kc.cuda(), vc.cuda(), bi.cuda(), bc.cuda(), seq.cuda(), block)
+    torch.cuda.synchronize()
+    ref = AO.sparse_decode_fp32(q, kc, vc, bi, bc, seq, block)
+    _close(out, ref)
+
+
+def test_no_device_timeouts_recorded(K):
+    assert K.device_status(clear=True) == 0
