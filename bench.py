@@ -1,0 +1,557 @@
+#!/usr/bin/env python
+"""Prefill benchmark of the block-sparse attention path on B200.
+
+Workload (default ``c1``): a deepseek-coder-1.3B-architecture LLaMA (24
+layers, hidden 2048, 16 heads x 128, MLP 5504, vocab 32256, RoPE theta 1e5
+linear x4), random-init bf16 weights, one 12288-token prompt of uniform random
+ids per GPU with seeded structure spans; every layer runs the block-sparse
+prefill kernel with block 64, a 4-block window, sink block, 128-token chunk
+groups and the per-layer pooled top-8 blocks. A step is one full-model
+prefill (logits for the last position, as generation's prefill computes).
+
+``value`` is prompt tokens/s over all ranks (weak scaling: one prompt per
+GPU, no collective on the data path). ``attn_tflops`` counts only listed
+(non-masked) 64x64 blocks, 4*64*64*128 FLOP each. Other workloads:
+``c2`` (8 prompts of 12288-16384 tokens split over the ranks, strong
+scaling), ``c3`` (6.7B architecture, 16384 tokens), ``c0`` (the single
+attention op, B=1, H=16, L=4096).
+
+``--impl reference`` times the reference's own CPU path for the same
+workload on the host cores: the dense-masked attention arithmetic of the
+reference's fallback (sabrecoder_attention_triton.py:2061-2066) inside a
+decoder layer, on a bounded sample (one decoder layer, scaled to the model).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "prefill tokens/s & effective sparse-attn TFLOP/s at 12K-16K ctx, 1/2/4/8 B200"
+
+ARCH = {
+    "1.3b": dict(vocab_size=32256, hidden_size=2048, intermediate_size=5504, num_hidden_layers=24,
+                 num_attention_heads=16, num_key_value_heads=16),
+    "6.7b": dict(vocab_size=32256, hidden_size=4096, intermediate_size=11008, num_hidden_layers=32,
+                 num_attention_heads=32, num_key_value_heads=32),
+}
+MASK = dict(block_size=64, window_size=192, num_prefix_tokens=64, num_suffix_tokens=128, max_chunk_tokens=128,
+            global_last_k_chunks=0)
+TOPK = 8
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c0"], default="c1")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attn-only", action="store_true",
+                    help="time the prefill attention kernel alone on one layer of the workload")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# workload definition
+# ---------------------------------------------------------------------------
+
+def workload(name: str, rank: int, world: int):
+    """Per-rank list of (prompt_len, seed) and the model architecture."""
+    if name == "c1":
+        return "1.3b", [(12288, 1000 + rank)], "weak"
+    if name == "c3":
+        return "6.7b", [(16384, 3000 + rank)], "weak"
+    if name == "c2":
+        import numpy as np
+        lens = np.random.default_rng(2).integers(12288, 16385, size=8).tolist()
+        order = sorted(range(8), key=lambda i: -lens[i])  # LPT over ranks
+        loads = [0] * world
+        mine = []
+        for i in order:
+            r = min(range(world), key=lambda j: loads[j])
+            loads[r] += lens[i]
+            if r == rank:
+                mine.append((int(lens[i]), 2000 + i))
+        return "1.3b", mine, "strong"
+    return None, [(4096, 0)], "weak"
+
+
+def build_model(arch: str, device):
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(**ARCH[arch], head_dim=128, max_position_embeddings=16384, rope_theta=100000.0,
+                      rope_scaling={"rope_type": "linear", "factor": 4.0}, rms_norm_eps=1e-6,
+                      tie_word_embeddings=False, attn_implementation="sdpa")
+    torch.manual_seed(0)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(device):
+            model = LlamaForCausalLM(cfg)
+    finally:
+        torch.set_default_dtype(prev)
+    return model.eval(), cfg
+
+
+def prompt_inputs(L: int, seed: int, vocab: int = 32256):
+    import numpy as np
+    from sabrecoder_b200.spans import BENCH_SPAN_MIX, make_spans
+    ids = np.random.default_rng(seed).integers(0, vocab, size=(1, L), dtype=np.int64)
+    spans = make_spans(L, seed, **BENCH_SPAN_MIX)
+    return ids, spans
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sms, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sms.append(float(p[1]))
+                mx = float(p[2])
+                power.append(float(p[3]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, p[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sms),
+                "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------------------
+# profiles/ figures (ncu summary committed next to this script)
+# ---------------------------------------------------------------------------
+
+def profile_traffic(kernel_tag: str):
+    """Per-launch DRAM bytes from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", f"{kernel_tag}.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return d.get("bf16_tflops"), d.get("bf16_tflops_sustained"), d.get("hbm_gbs"), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU side (reference arm and cpu_baseline)
+# ---------------------------------------------------------------------------
+
+def cpu_layer_sample(arch: str, L: int, seed: int, repeats: int = 1):
+    """One decoder layer of the workload on the host cores with the reference's
+    dense-masked attention arithmetic; returns (list of seconds per layer call,
+    layers, threads). Structure lists and pooled top-8 come from the oracle."""
+    import numpy as np
+    import torch
+    from oracle import attention_oracle as AO
+    from oracle import mask_oracle as MO
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaDecoderLayer, LlamaRotaryEmbedding
+    torch.set_num_threads(os.cpu_count() or 1)
+    threads = torch.get_num_threads()
+    a = ARCH[arch]
+    cfg = LlamaConfig(**a, head_dim=128, max_position_embeddings=16384, rope_theta=100000.0,
+                      rope_scaling={"rope_type": "linear", "factor": 4.0}, rms_norm_eps=1e-6)
+    torch.manual_seed(0)
+    layer = LlamaDecoderLayer(cfg, 0).float().eval()
+    rot = LlamaRotaryEmbedding(cfg)
+    _, spans = prompt_inputs(L, seed)
+    base = MO.build_block_mask_tokens(spans.token_to_chunk(), len(spans.spans), spans.import_chunks, spans.deps,
+                                      spans.signature_token_mask(), seq_len=L, **MASK).astype(bool)
+    B = MASK["block_size"]
+    attn = layer.self_attn
+
+    class DenseMasked(torch.nn.Module):
+        def forward(self, hidden_states, position_embeddings=None, **kw):
+            from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+            b, l = hidden_states.shape[:2]
+            shp = (b, l, -1, 128)
+            q = attn.q_proj(hidden_states).view(shp).transpose(1, 2)
+            k = attn.k_proj(hidden_states).view(shp).transpose(1, 2)
+            v = attn.v_proj(hidden_states).view(shp).transpose(1, 2)
+            q, k = apply_rotary_pos_emb(q, k, *position_embeddings)
+            qm = MO.pooled_block_means(q.detach().numpy(), l, B)
+            km = MO.pooled_block_means(k.detach().numpy(), l, B)
+            ext = MO.topk_extend_mask(base, MO.pooled_scores(qm, km), TOPK)
+            outs = []
+            for h in range(q.shape[1]):  # one head at a time bounds host memory
+                outs.append(AO.dense_masked_sdpa(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1],
+                                                 torch.from_numpy(ext[0, h]), B))
+            o = torch.cat(outs, 1).transpose(1, 2).reshape(b, l, -1)
+            return attn.o_proj(o), None
+
+    layer.self_attn = DenseMasked()
+    x = torch.randn(1, L, a["hidden_size"], generator=torch.Generator().manual_seed(seed)) * 0.02
+    pos = torch.arange(L).unsqueeze(0)
+    dts = []
+    with torch.no_grad():
+        pe = rot(x, pos)
+        for _ in range(repeats):
+            t0 = time.perf_counter()
+            layer(x, position_embeddings=pe, attention_mask=None)
+            dts.append(time.perf_counter() - t0)
+    return dts, a["num_hidden_layers"], threads
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    arch, prompts, scaling = workload(args.workload, 0, 1)
+    arch = arch or "1.3b"
+    L, seed = prompts[0]
+    # warm-up calls are folded into the same sample run and discarded
+    dts, layers, threads = cpu_layer_sample(arch, L, seed, repeats=min(args.warmup, 1) + args.steps)
+    times = [d * layers for d in dts[min(args.warmup, 1):]]
+    per_prompt = statistics.mean(times)
+    value = L / per_prompt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_prompt * 1e3, "higher_is_better": True,
+        "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {arch} LLaMA prefill, {L} tokens, block 64, "
+                               "structure spans + pooled top-8", "seq_len": L, "global_batch": 1},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"1 of {layers} decoder layers (fp32, dense-masked SDPA per head) on {L} "
+                                   f"tokens, scaled x{layers}; embeddings/lm_head excluded"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank, world, dist):
+    import numpy as np
+    import torch
+    from sabrecoder_b200 import kernels as K
+    from sabrecoder_b200 import sabrecoder_llama as SL
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    arch, prompts, scaling = workload(args.workload, rank, world)
+    if arch is None or args.attn_only:
+        return run_op_bench(args, rank, world, dist)
+    model, cfg = build_model(arch, dev)
+    SL.patch_model_with_sabrecoder_attention(model, None, topk_blocks=TOPK, verbose=False, **MASK)
+    mb = StructureAwareMaskBuilder(None, **MASK)
+    SL.set_current_code("<synthetic prompt>")
+
+    prepared = []
+    for L, seed in prompts:
+        ids, spans = prompt_inputs(L, seed, cfg.vocab_size)
+        bi, bc, bm = mb.build_block_indices_from_spans(spans, dev)
+        prepared.append((L, torch.from_numpy(ids).to(dev), bi, bc, bm, ids, spans))
+    tokens_per_step = sum(p[0] for p in prepared)
+
+    def step():
+        for L, ids_d, bi, bc, bm, _, _ in prepared:
+            SL.set_precomputed_blocks(bi, bc)
+            model(input_ids=ids_d, logits_to_keep=1)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            step()
+        barrier()
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        phys = vis.split(",")[dev.index] if vis else str(dev.index)
+        clocks = ClockSampler(int(phys) if phys.isdigit() else dev.index)
+        clocks.start()
+        events = K.set_prefill_timing(True)
+        launches0 = K.LAUNCHES[0]
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        barrier()
+        K.set_prefill_timing(False)
+        launches = K.LAUNCHES[0] - launches0
+        ck = clocks.stop()
+        ms = s.elapsed_time(e)
+        # attention kernel: per-launch algorithmic FLOPs over event durations
+        kt, kf = 0.0, 0.0
+        for a, b, cnt, heads, blk in events:
+            kt += a.elapsed_time(b)
+            kf += float(cnt.sum().item()) * heads * 4 * blk * blk * 128
+        nlaunch = max(len(events), 1)
+        dens = []
+        for L, _, bi, bc, bm, _, _ in prepared:
+            nb = bm.shape[0]
+            dens.append(float(bm.sum().item()) / (nb * (nb + 1) / 2))
+
+    ms_max = ms
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = tokens_per_step * world * args.steps / (ms_max / 1e3) if scaling == "weak" else None
+    if scaling == "strong":
+        tot = torch.tensor([tokens_per_step], device=dev, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(tot)
+        value = float(tot.item()) * args.steps / (ms_max / 1e3)
+
+    # end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_through_api(model, mb, prepared, args, dev, dist)
+
+    burst, sustained, hbm, which = measured_peaks()
+    per_launch_flop = kf / nlaunch
+    per_launch_ms = kt / nlaunch
+    achieved = per_launch_flop / (per_launch_ms * 1e-3) / 1e12 if per_launch_ms > 0 else 0.0
+    traffic = profile_traffic(f"prefill_bsa_{args.workload}")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        L0, seed0 = prompts[0]
+        dts, layers, threads = cpu_layer_sample(arch, L0, seed0)
+        v = L0 / (dts[0] * layers)
+        cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"1 of {layers} decoder layers (fp32, dense-masked SDPA per head) on {L0} tokens, "
+                         f"scaled x{layers}; embeddings/lm_head excluded"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{args.workload}: {arch} LLaMA (random-init bf16) sparse prefill, "
+                                   f"{'+'.join(str(p[0]) for p in prepared)} tokens per GPU, block 64, window 192, "
+                                   f"sink 64, suffix 128, 128-token chunk groups, pooled top-{TOPK} per layer/head",
+                       "seq_len": prepared[0][0], "global_batch": len(prompts) * (world if scaling == "weak" else 1),
+                       "parallelism": f"prompt-parallel x{world}, no collectives",
+                       "l2": "inputs larger than L2 (2.6 GB of weights read per step)",
+                       "density": round(statistics.mean(dens), 4)},
+            "attn_tflops": kf / (kt * 1e-3) / 1e12 if kt > 0 else None,
+            "attn_ms_per_step": kt / args.steps,
+            "roofline": {"kernel": "sabre prefill_bsa_kernel", "bound": "tensor", "achieved": achieved,
+                         "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained if sustained else None,
+                         "peak_kind": f"{which} bf16 dense, sustained (kernel timed inside a long step)",
+                         "flop_per_launch": per_launch_flop, "ms_per_launch": per_launch_ms,
+                         "traffic": traffic},
+            "gpu_launches": launches,
+            "clocks": ck,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def e2e_through_api(model, mb, prepared, args, dev, dist):
+    """tokens/s through the user-facing calls, with host inputs: each step
+    copies the prompt ids and the token-level structure from pinned host
+    memory, builds the block lists on the GPU, runs the patched model and
+    reads the last-position logits back."""
+    import numpy as np
+    import torch
+    from sabrecoder_b200 import sabrecoder_llama as SL
+    host = []
+    for L, _, _, _, _, ids, spans in prepared:
+        ptr, idx = spans.deps_csr()
+        arrs = dict(ids=torch.from_numpy(ids).pin_memory(),
+                    t2c=torch.from_numpy(spans.token_to_chunk()).pin_memory(),
+                    flags=torch.tensor([1 if s.tag == "import" else 0 for s in spans.spans],
+                                       dtype=torch.uint8).pin_memory(),
+                    ptr=torch.from_numpy(ptr).pin_memory(), idx=torch.from_numpy(idx).pin_memory(),
+                    gtm=torch.from_numpy(spans.signature_token_mask()).pin_memory())
+        host.append((L, arrs))
+    h2d = sum(sum(t.numel() * t.element_size() for t in a.values()) for _, a in host)
+    d2h = 0
+
+    def step():
+        nonlocal d2h
+        d2h = 0
+        for L, a in host:
+            d = {k: v.to(dev, non_blocking=True) for k, v in a.items()}
+            bits, dense = mb.build_block_mask_tokens(d["t2c"], d["flags"], d["ptr"], d["idx"], d["gtm"], L, dev)
+            bi, bc = mb._indices_from_bits(bits, dense.shape[0], 1)
+            SL.set_precomputed_blocks(bi, bc)
+            logits = model(input_ids=d["ids"], logits_to_keep=1).logits
+            out = logits.to("cpu")
+            d2h += out.numel() * out.element_size()
+
+    with torch.no_grad():
+        for _ in range(max(1, args.warmup)):
+            step()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    toks = sum(L for L, _ in host)
+    world = dist.get_world_size() if dist is not None else 1
+    _, _, scaling = workload(args.workload, 0, world)
+    if scaling == "weak":
+        val = toks * world * args.steps / (ms / 1e3)
+    else:
+        tt = torch.tensor([toks], device=dev, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(tt)
+        val = float(tt.item()) * args.steps / (ms / 1e3)
+    return {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+OP_SHAPES = {"c0": (16, 4096, "spans"), "c1": (16, 12288, "bench"), "c2": (16, 16384, "bench"),
+             "c3": (32, 16384, "bench")}
+
+
+def run_op_bench(args, rank, world, dist):
+    """The prefill attention op alone on one layer's shape of the workload
+    (c0: B=1, H=16, L=4096; c1: H=16, L=12288; c3: H=32, L=16384), block 64,
+    structure + pooled top-8 lists, L2 flushed between timed launches."""
+    import torch
+    from sabrecoder_b200 import kernels as K
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+    from sabrecoder_b200.spans import BENCH_SPAN_MIX, make_spans
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    H, L, mix = OP_SHAPES[args.workload]
+    blk = 64
+    g = torch.Generator(device=dev).manual_seed(rank)
+    q, k, v = (torch.randn(1, L, H, 128, device=dev, generator=g, dtype=torch.bfloat16).transpose(1, 2)
+               for _ in range(3))
+    mb = StructureAwareMaskBuilder(None, **MASK)
+    spans = make_spans(L, rank) if mix == "spans" else make_spans(L, 1000 + rank, **BENCH_SPAN_MIX)
+    bi, bc, bm = mb.build_block_indices_from_spans(spans, dev)
+    qm, km = K.pool_blocks(q, blk), K.pool_blocks(k, blk)
+    idx, cnt, mx, _ = K.topk_extend(qm, km, mb.last_block_bits, TOPK)
+    ma = int(mx.item())
+    idx = idx[..., :ma].contiguous()
+    out = torch.empty_like(q)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        K.prefill_bsa(q, k, v, idx, cnt, blk, out=out)
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        K.prefill_bsa(q, k, v, idx, cnt, blk, out=out)
+        e.record()
+        torch.cuda.synchronize()
+        tot += s.elapsed_time(e)
+    ms = tot / args.steps
+    flop = float(cnt.sum().item()) * 4 * blk * blk * 128
+    nb = bm.shape[0]
+    dens = float(cnt.sum().item()) / (H * nb * (nb + 1) / 2)
+    burst, sustained, hbm, which = measured_peaks()
+    traffic = profile_traffic(f"prefill_bsa_{args.workload}_op")
+    if rank == 0:
+        print(json.dumps({"metric": "effective sparse-attn TFLOP/s (single op)", "value": flop / ms / 1e9,
+                          "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "bf16", "data": "synthetic",
+                          "config": {"workload": f"{args.workload} attention op: B=1 H={H} L={L} D=128 block 64, "
+                                                 f"structure + top-{TOPK}, density {dens:.4f}",
+                                     "l2": "L2 flushed (256 MB write) between iterations"},
+                          "roofline": {"kernel": "sabre prefill_bsa_kernel", "bound": "tensor",
+                                       "achieved": flop / ms / 1e9, "peak": burst, "unit": "TFLOP/s",
+                                       "frac": flop / ms / 1e9 / burst, "peak_kind": f"{which} bf16 dense, burst",
+                                       "flop_per_launch": flop, "ms_per_launch": ms, "traffic": traffic}}))
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dist = None
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+    import torch
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist = tdist
+    try:
+        run_ours(args, rank, world, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

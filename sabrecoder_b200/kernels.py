@@ -17,6 +17,18 @@ from ._lib import SabreError, check, i64, lib
 
 DTYPE_CODE = {torch.bfloat16: 0, torch.float16: 1}
 
+# Number of CUDA kernels launched through this module (cumulative).
+LAUNCHES = [0]
+# When a list, prefill_bsa appends (start_event, end_event, block_counts,
+# heads) per launch so callers can time the kernel on its own stream.
+PREFILL_EVENTS = None
+
+
+def set_prefill_timing(on: bool):
+    global PREFILL_EVENTS
+    PREFILL_EVENTS = [] if on else None
+    return PREFILL_EVENTS
+
 
 def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
@@ -75,11 +87,19 @@ def prefill_bsa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_indices
         raise SabreError(f"index lists {tuple(bi.shape)} / counts {tuple(bc.shape)} do not match B={B}, nb={nb}")
     if out is None:
         out = torch.empty_like(q)
+    ev = None
+    if PREFILL_EVENTS is not None:
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record(torch.cuda.current_stream(q.device))
     st = lib().sabre_prefill_bsa(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), bi.data_ptr(), bc.data_ptr(), B, Hq, Hkv, L, D,
         int(block_size), int(bi.shape[-1]), i64(q.stride()), i64(k.stride()), i64(v.stride()), i64(out.stride()),
         i64(idx_strides), i64(cnt_strides), float(softmax_scale or 0.0), DTYPE_CODE[q.dtype], _stream(q))
     check(st, "sabre_prefill_bsa")
+    LAUNCHES[0] += 1
+    if ev is not None:
+        ev[1].record(torch.cuda.current_stream(q.device))
+        PREFILL_EVENTS.append((ev[0], ev[1], bc, Hq if bi.dim() == 3 or bi.shape[1] == 1 else 1, int(block_size)))
     return out
 
 
@@ -128,6 +148,7 @@ def decode_bsa(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, bl
         float(softmax_scale or 0.0), DTYPE_CODE[q.dtype], workspace.data_ptr(),
         workspace.numel() * workspace.element_size(), _stream(q))
     check(st, "sabre_decode_bsa")
+    LAUNCHES[0] += 2
     return out
 
 
@@ -161,6 +182,7 @@ def build_block_mask(token_to_chunk: torch.Tensor, chunk_flags: torch.Tensor, de
         int(window_size), int(num_prefix_tokens), int(num_suffix_tokens), int(max_chunk_tokens),
         int(global_last_k_chunks), bits.data_ptr(), _ptr(dm), ws.data_ptr(), ws.numel(), _stream(bits))
     check(st, "sabre_build_block_mask")
+    LAUNCHES[0] += 2
     return bits, dm
 
 
@@ -177,6 +199,7 @@ def indices_from_bits(bits: torch.Tensor, ncols: int, cap: Optional[int] = None)
     mx = torch.empty(1, dtype=torch.int32, device=bits.device)
     check(lib().sabre_indices_from_bits(b.data_ptr(), rows, int(ncols), idx.data_ptr(), cap, cnt.data_ptr(),
                                         mx.data_ptr(), _stream(bits)), "sabre_indices_from_bits")
+    LAUNCHES[0] += 1
     return idx.reshape(*lead, cap), cnt.reshape(lead), mx
 
 
@@ -197,6 +220,7 @@ def indices_from_dense(mask: torch.Tensor, cap: Optional[int] = None):
     mx = torch.empty(1, dtype=torch.int32, device=m.device)
     check(lib().sabre_indices_from_dense(m2.data_ptr(), rows, ncols, m2.stride(0), idx.data_ptr(), cap,
                                          cnt.data_ptr(), mx.data_ptr(), _stream(m)), "sabre_indices_from_dense")
+    LAUNCHES[0] += 1
     return idx.reshape(*lead, cap), cnt.reshape(lead), mx
 
 
@@ -209,6 +233,7 @@ def pool_blocks(x: torch.Tensor, block_size: int) -> torch.Tensor:
     out = torch.empty(B, H, nb, D, dtype=torch.float32, device=x.device)
     check(lib().sabre_pool_blocks(x.data_ptr(), B, H, L, D, int(block_size), i64(x.stride()), DTYPE_CODE[x.dtype],
                                   out.data_ptr(), _stream(x)), "sabre_pool_blocks")
+    LAUNCHES[0] += 1
     return out
 
 
@@ -230,6 +255,7 @@ def topk_extend(q_pooled: torch.Tensor, k_pooled: torch.Tensor, base_bits: torch
     check(lib().sabre_topk_extend(qp.data_ptr(), kp.data_ptr(), bb.data_ptr(), B, Hq, Hkv, nb, D, int(topk),
                                   idx.data_ptr(), cap, cnt.data_ptr(), mx.data_ptr(), _ptr(ob), _stream(qp)),
           "sabre_topk_extend")
+    LAUNCHES[0] += 1
     return idx, cnt, mx, ob
 
 

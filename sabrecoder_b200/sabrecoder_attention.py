@@ -1,0 +1,559 @@
+"""Structure-aware block-sparse attention: mask builder and attention module.
+
+Drop-in counterpart of methods/sabrecoder/sabrecoder_attention_triton.py.
+Same class and function names, constructor arguments, validation errors and
+return types; the arithmetic runs in libsabre_b200.so on the GPU:
+
+* ``StructureAwareMaskBuilder`` (reference :229-1828): text-level work stays
+  on the host (tokenizer offsets -> lines -> chunks, signature and special
+  lines); the block mask (rules R0-R3, :1455-1604) and the index lists
+  (:1837-1859) are built by CUDA kernels.
+* ``compute_block_indices_from_mask`` (:1837-1859): CUDA kernel; rows are
+  ascending (the reference's unstable argsort leaves them unordered; counts
+  and per-row sets are identical).
+* ``StructureAwareSparseAttention`` (:1890-2072): same dispatch as the
+  reference's ``forward``; the sparse path calls the tcgen05 prefill kernel.
+  Optional ``topk_blocks`` adds, per layer and head, the top-k key blocks by
+  pooled q.k (no reference counterpart).
+
+Tree-sitter segmentation and the reference graph (semantic_chunker.py,
+reference_graph.py) are pluggable: pass ``segmenter_factory`` /
+``analyzer_factory`` (same interfaces as the reference classes) or call the
+``*_from_chunks`` / ``*_from_spans`` entry points with ready-made structure.
+"""
+
+from __future__ import annotations
+
+import math
+import re
+from collections import OrderedDict
+from typing import Dict, Iterable, List, Optional, Sequence, Set, Tuple
+
+import numpy as np
+import torch
+import torch.nn as nn
+
+from . import kernels as K
+from .chunks import SIGNATURE_TYPES, ChunkType, CodeChunk, type_name
+
+_GLOBAL_CHUNK_CACHE: "OrderedDict" = OrderedDict()
+_GLOBAL_LINE_TO_TOKEN_CACHE: "OrderedDict" = OrderedDict()
+_GLOBAL_MASK_CACHE: "OrderedDict" = OrderedDict()
+_BLOCK_MASK_CACHE: "OrderedDict" = OrderedDict()
+_GLOBAL_CACHE_MAX_SIZE = 50
+
+
+def _cache_put(cache: OrderedDict, key, value, cap: int = _GLOBAL_CACHE_MAX_SIZE) -> None:
+    if key in cache:
+        cache.move_to_end(key)
+    cache[key] = value
+    while len(cache) > cap:
+        cache.popitem(last=False)
+
+
+def _char_to_line(code: str) -> np.ndarray:
+    lens = np.fromiter((len(s) + 1 for s in code.split("\n")), dtype=np.int64)
+    return np.repeat(np.arange(1, lens.shape[0] + 1, dtype=np.int64), lens)
+
+
+def _token_starts(enc, seq_len: int) -> np.ndarray:
+    offs = enc.get("offset_mapping")
+    ids = enc.get("input_ids")
+    if offs is None or ids is None:
+        raise RuntimeError("Tokenizer must support return_offsets_mapping and return input_ids for token mapping.")
+    n = min(seq_len, len(ids))
+    st = np.full(n, -1, dtype=np.int64)
+    for t in range(n):
+        s = offs[t][0]
+        if s is not None and s >= 0:
+            st[t] = s
+    return st
+
+
+def bits_from_indices(block_indices: torch.Tensor, block_counts: torch.Tensor, ncols: int) -> torch.Tensor:
+    """Row bitsets (int32 words, uint32 semantics) from index lists
+    ``[..., max]`` + counts ``[...]``: entries below the count in ``[0, ncols)``."""
+    idx = block_indices.long()
+    ar = torch.arange(idx.shape[-1], device=idx.device)
+    ok = (ar < block_counts.long().unsqueeze(-1)) & (idx >= 0) & (idx < ncols)
+    nwords = (ncols + 31) // 32
+    m = torch.zeros(idx.shape[:-1] + (nwords * 32 + 1,), dtype=torch.bool, device=idx.device)
+    m.scatter_(-1, torch.where(ok, idx, torch.full_like(idx, nwords * 32)), True)
+    m = m[..., : nwords * 32].reshape(idx.shape[:-1] + (nwords, 32)).to(torch.int64)
+    w = (m << torch.arange(32, device=idx.device, dtype=torch.int64)).sum(-1)
+    return torch.where(w >= 2 ** 31, w - 2 ** 32, w).to(torch.int32)
+
+
+class StructureAwareMaskBuilder:
+    """Block mask / index-list builder (reference
+    sabrecoder_attention_triton.py:229-1828)."""
+
+    def __init__(self, tokenizer, window_size=64, num_prefix_tokens=128, num_suffix_tokens=256,
+                 block_size: int = 64, global_last_k_chunks: int = 2, max_chunk_tokens: int = 0,
+                 embedding_weight: Optional[torch.Tensor] = None, use_chunk_similarity: bool = False,
+                 chunk_similarity_top_percent: float = 0.1, chunk_similarity_max_tokens_per_chunk: int = 256,
+                 chunk_similarity_max_neighbors: int = 8, use_crossfile_chunk_similarity: bool = False,
+                 crossfile_chunk_similarity_top_percent: Optional[float] = None, *,
+                 device: Optional[torch.device] = None, segmenter_factory=None, analyzer_factory=None):
+        self.tokenizer = tokenizer
+        self.window_size = window_size
+        self.num_prefix_tokens = num_prefix_tokens
+        self.num_suffix_tokens = num_suffix_tokens
+        self.block_size = int(block_size)
+        self.global_last_k_chunks = int(global_last_k_chunks)
+        self.max_chunk_tokens = int(max_chunk_tokens)
+        self.embedding_weight = embedding_weight
+        self.use_chunk_similarity = bool(use_chunk_similarity)
+        self.chunk_similarity_top_percent = float(chunk_similarity_top_percent)
+        self.chunk_similarity_max_tokens_per_chunk = int(chunk_similarity_max_tokens_per_chunk)
+        self.chunk_similarity_max_neighbors = int(chunk_similarity_max_neighbors)
+        self.use_crossfile_chunk_similarity = bool(use_crossfile_chunk_similarity)
+        self.crossfile_chunk_similarity_top_percent = (
+            float(crossfile_chunk_similarity_top_percent) if crossfile_chunk_similarity_top_percent is not None
+            else float(chunk_similarity_top_percent))
+        self.device = device
+        self.segmenter_factory = segmenter_factory
+        self.analyzer_factory = analyzer_factory
+        self.last_block_bits: Optional[torch.Tensor] = None
+        # Validation mirrors sabrecoder_attention_triton.py:268-292.
+        if self.block_size <= 0:
+            raise ValueError("block_size must be > 0.")
+        if self.global_last_k_chunks < 0:
+            raise ValueError("global_last_k_chunks must be >= 0.")
+        if self.max_chunk_tokens < 0:
+            raise ValueError("max_chunk_tokens must be >= 0.")
+        if self.max_chunk_tokens > 0 and (self.max_chunk_tokens % self.block_size) != 0:
+            raise ValueError("max_chunk_tokens must be a multiple of block_size to align with kernel blocks.")
+        if self.use_crossfile_chunk_similarity and not self.use_chunk_similarity:
+            raise ValueError("use_crossfile_chunk_similarity=True requires use_chunk_similarity=True.")
+        if self.use_chunk_similarity:
+            if self.embedding_weight is None:
+                raise ValueError("use_chunk_similarity=True requires embedding_weight "
+                                 "(model.get_input_embeddings().weight).")
+            if self.chunk_similarity_top_percent < 0.0:
+                raise ValueError("chunk_similarity_top_percent must be >= 0.")
+            if self.chunk_similarity_max_tokens_per_chunk <= 0:
+                raise ValueError("chunk_similarity_max_tokens_per_chunk must be > 0.")
+            if self.chunk_similarity_max_neighbors < 0:
+                raise ValueError("chunk_similarity_max_neighbors must be >= 0.")
+            if self.use_crossfile_chunk_similarity and self.crossfile_chunk_similarity_top_percent < 0.0:
+                raise ValueError("crossfile_chunk_similarity_top_percent must be >= 0.")
+
+    # ------------------------------------------------------------------
+    # Host text processing (reference :407-456, :697-858)
+    # ------------------------------------------------------------------
+    def _encode(self, code: str, seq_len: int):
+        return self.tokenizer(code, add_special_tokens=True, truncation=True, max_length=seq_len,
+                              return_offsets_mapping=True)
+
+    def _get_token_to_line_mapping(self, code: str, seq_len: int) -> List[int]:
+        """Token -> 1-based line, 0 for tokens without an offset (:407-447)."""
+        key = (hash(code), seq_len)
+        hit = _GLOBAL_LINE_TO_TOKEN_CACHE.get(key)
+        if hit is not None:
+            return hit
+        starts = _token_starts(self._encode(code, seq_len), seq_len)
+        c2l = _char_to_line(code)
+        out = np.zeros(seq_len, dtype=np.int64)
+        ok = starts >= 0
+        out[: starts.shape[0]][ok] = c2l[np.minimum(starts[ok], c2l.shape[0] - 1)]
+        res = out.tolist()
+        _cache_put(_GLOBAL_LINE_TO_TOKEN_CACHE, key, res)
+        return res
+
+    def _map_lines_to_tokens(self, code: str, line_numbers: set, seq_len: int) -> torch.Tensor:
+        """bool [seq_len]: token lies on one of ``line_numbers`` (:449-456)."""
+        if not line_numbers:
+            return torch.zeros(seq_len, dtype=torch.bool)
+        t2l = np.asarray(self._get_token_to_line_mapping(code, seq_len))
+        lines = np.fromiter(line_numbers, dtype=np.int64)
+        return torch.from_numpy(np.isin(t2l, lines))
+
+    def _identify_special_lines(self, code: str, chunks, language: Optional[str] = None) -> dict:
+        """Python-only globally visible lines (:697-752): module-level
+        assignments, type aliases, ``self.x =`` in ``__init__``, returns."""
+        empty = {"global_vars": set(), "type_aliases": set(), "class_attrs": set(), "return_stmts": set()}
+        if language is None or str(language).lower() not in {"python", "py"}:
+            return empty
+        fc: Set[int] = set()
+        init: Set[int] = set()
+        for ch in chunks:
+            tn = type_name(ch.chunk_type)
+            if tn in SIGNATURE_TYPES:
+                fc.update(range(ch.start_line, ch.end_line + 1))
+            if tn == "METHOD" and getattr(ch, "name", "") == "__init__":
+                init.update(range(ch.start_line, ch.end_line + 1))
+        res = {k: set() for k in empty}
+        assign = re.compile(r"^[A-Za-z_][A-Za-z0-9_]*\s*[:\[]?\s*=")
+        alias = re.compile(r"^[A-Z][A-Za-z0-9_]*\s*=\s*[A-Z][A-Za-z0-9_]*\[")
+        attr = re.compile(r"^\s*self\.[A-Za-z_][A-Za-z0-9_]*\s*=")
+        ret = re.compile(r"^\s*return\b")
+        skip = ("==", "!=", "<=", ">=", "def ", "class ", "import ", "from ")
+        for n, line in enumerate(code.split("\n"), start=1):
+            s = line.strip()
+            if not s or s.startswith("#"):
+                continue
+            if n not in fc and "=" in s and not any(w in s for w in skip) and assign.match(s):
+                res["global_vars"].add(n)
+            if "TypeAlias" in s or alias.match(s):
+                res["type_aliases"].add(n)
+            if n in init and attr.match(line):
+                res["class_attrs"].add(n)
+            if n in fc and ret.match(s):
+                res["return_stmts"].add(n)
+        return res
+
+    def _append_uncovered_line_chunks(self, code: str, chunks: List) -> List:
+        """Append MODULE_CODE chunks for maximal runs of lines no chunk covers
+        (:754-805); existing chunk indices stay stable."""
+        if not code:
+            return chunks
+        lines = code.split("\n")
+        n = len(lines)
+        if n <= 0:
+            return chunks
+        covered = np.zeros(n + 1, dtype=bool)
+        for ch in chunks or []:
+            s = max(1, int(getattr(ch, "start_line", 1) or 1))
+            e = min(n, int(getattr(ch, "end_line", 0) or 0))
+            if e >= s:
+                covered[s : e + 1] = True
+        out = list(chunks or [])
+        ln = 1
+        while ln <= n:
+            if covered[ln]:
+                ln += 1
+                continue
+            s = ln
+            while ln <= n and not covered[ln]:
+                ln += 1
+            text = "\n".join(lines[s - 1 : ln - 1])
+            out.append(CodeChunk(ChunkType.MODULE_CODE, 0, len(text), text, "", None, s, ln - 1, None, None))
+        return out
+
+    def _map_tokens_to_chunks(self, code: str, chunks, seq_len: int) -> List[int]:
+        """Token -> chunk through lines; the last chunk in list order wins for a
+        line (:807-858)."""
+        t2c = np.full(seq_len, -1, dtype=np.int64)
+        if not chunks:
+            return t2c.tolist()
+        nl = len(code.split("\n"))
+        l2c = np.full(nl + 1, -1, dtype=np.int64)
+        for ci, ch in enumerate(chunks):
+            s, e = int(ch.start_line), int(ch.end_line)
+            if s >= 0:
+                if s <= min(e, nl):
+                    l2c[s : min(e, nl) + 1] = ci
+            else:  # negative line numbers index from the end, as Python lists do
+                for ln in range(s, e + 1):
+                    if ln <= nl:
+                        l2c[ln] = ci
+        enc = self._encode(code, seq_len)
+        offs, ids = enc.get("offset_mapping"), enc.get("input_ids")
+        if offs is None or ids is None:
+            raise RuntimeError("Tokenizer must support return_offsets_mapping and return input_ids for token mapping.")
+        if len(offs) < len(ids):
+            raise RuntimeError("Tokenizer returned offset_mapping shorter than input_ids; cannot build stable mapping.")
+        if not ids:
+            return t2c.tolist()
+        starts = _token_starts(enc, seq_len)
+        c2l = _char_to_line(code)
+        ok = starts >= 0
+        lines = c2l[np.minimum(starts[ok], c2l.shape[0] - 1)]
+        head = t2c[: starts.shape[0]]
+        vals = np.where(lines < l2c.shape[0], l2c[np.minimum(lines, l2c.shape[0] - 1)], head[ok])
+        head[ok] = vals
+        return t2c.tolist()
+
+    # ------------------------------------------------------------------
+    # Token-level structure -> GPU
+    # ------------------------------------------------------------------
+    def structure_to_tokens(self, *, code: str, seq_len: int, chunks: Sequence, chunk_deps: Dict[int, Set[int]],
+                            import_chunks: Iterable[int], language: Optional[str]):
+        """Host arrays for the mask kernel: token_to_chunk int32[L], global
+        token mask uint8[L], chunk flags uint8[nchunks], dependency CSR."""
+        t2c = np.asarray(self._map_tokens_to_chunks(code, chunks, seq_len), dtype=np.int32)
+        vis: Set[int] = set()
+        for ch in chunks:
+            if type_name(ch.chunk_type) in SIGNATURE_TYPES:
+                s0 = getattr(ch, "signature_start_line", None)
+                s1 = getattr(ch, "signature_end_line", None)
+                if s0 and s1:
+                    vis.update(range(s0, s1 + 1))
+        sp = self._identify_special_lines(code, chunks, language=language)
+        for key in ("global_vars", "type_aliases", "class_attrs", "return_stmts"):
+            vis |= sp[key]
+        gtm = self._map_lines_to_tokens(code, vis, seq_len).numpy().astype(np.uint8)
+        n = len(chunks)
+        flags = np.zeros(n, dtype=np.uint8)
+        for c in import_chunks or ():
+            c = int(c)
+            if 0 <= c < n:
+                flags[c] |= 1
+        ptr, idx = deps_to_csr(chunk_deps, n)
+        return t2c, gtm, flags, ptr, idx
+
+    def build_block_mask_tokens(self, token_to_chunk, chunk_flags, dep_ptr, dep_idx, global_token_mask, seq_len,
+                                device=None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """GPU block mask from token-level structure: ``(bits, dense)``."""
+        dev = torch.device(device if device is not None else (self.device or "cuda"))
+
+        def up(a, dt):
+            if isinstance(a, torch.Tensor):
+                return a.to(device=dev, dtype=dt, non_blocking=True).contiguous()
+            return torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(dev, non_blocking=True)
+
+        return K.build_block_mask(
+            up(token_to_chunk, torch.int32), up(chunk_flags, torch.uint8), up(dep_ptr, torch.int32),
+            up(dep_idx, torch.int32), None if global_token_mask is None else up(global_token_mask, torch.uint8),
+            seq_len=int(seq_len), block_size=self.block_size, window_size=int(self.window_size),
+            num_prefix_tokens=int(self.num_prefix_tokens), num_suffix_tokens=int(self.num_suffix_tokens),
+            max_chunk_tokens=self.max_chunk_tokens, global_last_k_chunks=self.global_last_k_chunks)
+
+    def _build_block_mask_from_chunks(self, *, code: str, seq_len: int, chunks: List,
+                                      chunk_deps: Dict[int, Set[int]], import_chunks: Set[int],
+                                      language: Optional[str], device=None) -> torch.Tensor:
+        """int32 ``[nb, nb]`` block mask on the GPU (reference :1455-1604)."""
+        t2c, gtm, flags, ptr, idx = self.structure_to_tokens(code=code, seq_len=seq_len, chunks=chunks,
+                                                             chunk_deps=chunk_deps, import_chunks=import_chunks,
+                                                             language=language)
+        bits, dense = self.build_block_mask_tokens(t2c, flags, ptr, idx, gtm, seq_len, device)
+        self.last_block_bits = bits
+        return dense
+
+    # ------------------------------------------------------------------
+    # Index lists
+    # ------------------------------------------------------------------
+    def _indices_from_bits(self, bits: torch.Tensor, nb: int, batch_size: int):
+        idx, cnt, mx = K.indices_from_bits(bits, nb)
+        ma = int(mx.item())
+        bi = idx[:, :ma].unsqueeze(0).expand(int(batch_size), -1, -1).contiguous()
+        bc = cnt.unsqueeze(0).expand(int(batch_size), -1).contiguous()
+        return bi, bc
+
+    def build_block_indices_from_chunks(self, code: str, seq_len: int, device, *, chunks: List,
+                                        chunk_deps: Dict[int, Set[int]], import_chunks: Set[int],
+                                        language: Optional[str] = None, batch_size: int = 1):
+        dense = self._build_block_mask_from_chunks(code=code, seq_len=seq_len, chunks=chunks, chunk_deps=chunk_deps,
+                                                   import_chunks=import_chunks, language=language, device=device)
+        bi, bc = self._indices_from_bits(self.last_block_bits, dense.shape[0], batch_size)
+        return bi, bc, dense
+
+    def build_block_indices_from_spans(self, spanset, device=None, *, batch_size: int = 1):
+        """Index lists for seeded synthetic spans (token-level structure, no
+        text or tokenizer needed)."""
+        ptr, idx = spanset.deps_csr()
+        flags = np.asarray([1 if s.tag == "import" else 0 for s in spanset.spans], dtype=np.uint8)
+        bits, dense = self.build_block_mask_tokens(spanset.token_to_chunk(), flags, ptr, idx,
+                                                   spanset.signature_token_mask(), spanset.seq_len, device)
+        self.last_block_bits = bits
+        bi, bc = self._indices_from_bits(bits, dense.shape[0], batch_size)
+        return bi, bc, dense
+
+    def build_block_indices(self, code: str, seq_len: int, device, *, batch_size: int = 1,
+                            crossfile_code: Optional[str] = None, current_code: Optional[str] = None,
+                            language: Optional[str] = None, crossfile_full_attention: bool = True):
+        """``(block_indices int32 [B, nb, max_active], block_counts int32 [B, nb],
+        block_mask_2d int32 [nb, nb])`` on ``device`` (reference :1606-1819)."""
+        if crossfile_code is not None and current_code is not None:
+            raise NotImplementedError("cross-file prompt chunking (sabrecoder_attention_triton.py:1622-1772) is "
+                                      "not part of this library; segment the prompt and call "
+                                      "build_block_indices_from_chunks")
+        if self.use_chunk_similarity:
+            raise NotImplementedError("chunk-similarity edges are not implemented; pass use_chunk_similarity=False")
+        key = (hash(code), str(language).lower() if language else None)
+        hit = _GLOBAL_CHUNK_CACHE.get(key)
+        if hit is None:
+            seg, ana = self._structure_backends()
+            chunks = seg(tokenizer=self.tokenizer).segment_code(code, language=language)
+            imports = {i for i, c in enumerate(chunks) if type_name(c.chunk_type) == "IMPORT"}
+            deps: Dict[int, Set[int]] = {}
+            for ref in ana(chunks, code, language=language).analyze():
+                s, t = ref.source_chunk_idx, ref.target_chunk_idx
+                deps.setdefault(s, set()).add(t)
+                deps.setdefault(t, set()).add(s)
+            chunks = self._append_uncovered_line_chunks(code, chunks)
+            hit = {"chunks": chunks, "chunk_deps": deps, "import_chunks": imports}
+            _cache_put(_GLOBAL_CHUNK_CACHE, key, hit)
+        return self.build_block_indices_from_chunks(code, seq_len, device, chunks=hit["chunks"],
+                                                    chunk_deps=hit["chunk_deps"], import_chunks=hit["import_chunks"],
+                                                    language=language, batch_size=batch_size)
+
+    def _structure_backends(self):
+        seg, ana = self.segmenter_factory, self.analyzer_factory
+        if seg is None or ana is None:
+            try:
+                from semantic_chunker import TreeSitterSegmenter  # the reference's segmenter, if importable
+                from reference_graph import CrossReferenceAnalyzer
+            except Exception as e:  # noqa: BLE001
+                raise RuntimeError("code segmentation needs tree-sitter (semantic_chunker / reference_graph); pass "
+                                   "segmenter_factory/analyzer_factory or use build_block_indices_from_chunks") from e
+            seg = seg or TreeSitterSegmenter
+            ana = ana or CrossReferenceAnalyzer
+        return seg, ana
+
+    def clear_cache(self):
+        clear_all_caches()
+
+
+def deps_to_csr(chunk_deps: Optional[Dict[int, Iterable[int]]], nchunks: int):
+    """Dependency dict -> CSR (dep_ptr int32[nchunks+1], dep_idx int32[]),
+    dropping out-of-range sources and targets (the reference skips them,
+    :1530 and :1537)."""
+    ptr = np.zeros(nchunks + 1, dtype=np.int32)
+    flat: List[int] = []
+    deps = chunk_deps or {}
+    for c in range(nchunks):
+        tg = deps.get(c)
+        if tg:
+            flat.extend(sorted(int(t) for t in tg if 0 <= int(t) < nchunks))
+        ptr[c + 1] = len(flat)
+    return ptr, np.asarray(flat, dtype=np.int32)
+
+
+def compute_block_indices_from_mask(block_mask: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``(block_indices int32 [B, nb, max_active], block_counts int32 [B, nb])``
+    from a ``[B, nb_m, nb_n]`` mask (reference :1837-1859). Runs on the GPU;
+    CPU inputs are moved there and the results moved back."""
+    dev = block_mask.device
+    m = block_mask if block_mask.is_cuda else block_mask.to("cuda")
+    idx, cnt, mx = K.indices_from_dense(m)
+    ma = int(mx.item())
+    bi = idx[..., :ma].contiguous()
+    return bi.to(dev), cnt.to(dev)
+
+
+def compute_block_mask_from_token_mask(token_mask: torch.Tensor, block_size_m: int, block_size_n: int) -> torch.Tensor:
+    """Block (i, j) is active iff any token pair in it is not -inf
+    (reference :1862-1885). O(L^2) debugging helper; plain torch ops."""
+    L = token_mask.shape[0]
+    nbm = (L + block_size_m - 1) // block_size_m
+    nbn = (L + block_size_n - 1) // block_size_n
+    pm, pn = nbm * block_size_m - L, nbn * block_size_n - L
+    if pm or pn:
+        token_mask = torch.nn.functional.pad(token_mask, (0, pn, 0, pm), value=float("-inf"))
+    t = token_mask.view(nbm, block_size_m, nbn, block_size_n)
+    return (~torch.isinf(t)).any(dim=(1, 3)).to(torch.int32)
+
+
+class StructureAwareSparseAttention(nn.Module):
+    """Attention module (reference StructureAwareSparseAttentionTriton,
+    :1890-2072). ``forward(q, k, v, code=...)`` takes ``[B, H, L, D]`` tensors
+    (any strides with unit head-dim stride; K/V may have fewer heads)."""
+
+    def __init__(self, tokenizer, block_size=64, window_size=64, num_prefix_tokens=128, num_suffix_tokens=256,
+                 use_token_level_sparsity=False, embedding_weight: Optional[torch.Tensor] = None,
+                 global_last_k_chunks: int = 2, max_chunk_tokens: int = 0, use_chunk_similarity: bool = False,
+                 chunk_similarity_top_percent: float = 0.1, chunk_similarity_max_tokens_per_chunk: int = 256,
+                 chunk_similarity_max_neighbors: int = 8, use_crossfile_chunk_similarity: bool = False,
+                 crossfile_chunk_similarity_top_percent: Optional[float] = None, topk_blocks: int = 0,
+                 segmenter_factory=None, analyzer_factory=None):
+        super().__init__()
+        if use_token_level_sparsity:
+            raise NotImplementedError("the token-level sparse kernel variant is not implemented; "
+                                      "use block-level sparsity")
+        self.tokenizer = tokenizer
+        self.block_size = int(block_size)
+        self.window_size = window_size
+        self.num_prefix_tokens = num_prefix_tokens
+        self.num_suffix_tokens = num_suffix_tokens
+        self.use_token_level_sparsity = False
+        self.topk_blocks = int(topk_blocks)
+        self.mask_builder = StructureAwareMaskBuilder(
+            tokenizer=tokenizer, block_size=self.block_size, window_size=window_size,
+            num_prefix_tokens=num_prefix_tokens, num_suffix_tokens=num_suffix_tokens,
+            global_last_k_chunks=global_last_k_chunks, max_chunk_tokens=max_chunk_tokens,
+            embedding_weight=embedding_weight, use_chunk_similarity=use_chunk_similarity,
+            chunk_similarity_top_percent=chunk_similarity_top_percent,
+            chunk_similarity_max_tokens_per_chunk=chunk_similarity_max_tokens_per_chunk,
+            chunk_similarity_max_neighbors=chunk_similarity_max_neighbors,
+            use_crossfile_chunk_similarity=use_crossfile_chunk_similarity,
+            crossfile_chunk_similarity_top_percent=crossfile_chunk_similarity_top_percent,
+            segmenter_factory=segmenter_factory, analyzer_factory=analyzer_factory)
+
+    def _lookup_blocks(self, query, code, batch_size):
+        from .sabrecoder_llama import get_precomputed_blocks
+        gi, gc = get_precomputed_blocks()
+        if gi is not None and gc is not None:
+            return gi, gc
+        mb = self.mask_builder
+        key = (hash(code), query.shape[2], self.block_size, query.device, batch_size, mb.window_size,
+               mb.num_prefix_tokens, mb.num_suffix_tokens, mb.block_size, mb.global_last_k_chunks,
+               mb.max_chunk_tokens, mb.use_chunk_similarity)
+        hit = _BLOCK_MASK_CACHE.get(key)
+        if hit is None:
+            bi, bc, _ = mb.build_block_indices(code, query.shape[2], query.device, batch_size=batch_size)
+            hit = (bi, bc)
+            _cache_put(_BLOCK_MASK_CACHE, key, hit)
+        return hit
+
+    def forward(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, code: str = None,
+                attention_mask: Optional[torch.Tensor] = None,
+                precomputed_block_indices: Optional[torch.Tensor] = None,
+                precomputed_block_counts: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None
+                ) -> torch.Tensor:
+        B, H, Lq, D = query.shape
+        Lk = key.shape[2]
+        if code is not None and Lq == Lk and Lq > 1:
+            if precomputed_block_indices is not None and precomputed_block_counts is not None:
+                bi, bc = precomputed_block_indices, precomputed_block_counts
+            else:
+                bi, bc = self._lookup_blocks(query, code, B)
+            if self.topk_blocks > 0:
+                bi, bc = self.extend_topk(query, key, bi, bc)
+            return K.prefill_bsa(query, key, value, bi, bc, self.block_size, out=out)
+        # Dense path for everything else, as the reference does (:2056-2066).
+        if attention_mask is not None and attention_mask.shape[-2:] != (Lq, Lk):
+            attention_mask = None
+        if key.shape[1] != H:
+            g = H // key.shape[1]
+            key = key.repeat_interleave(g, dim=1)
+            value = value.repeat_interleave(g, dim=1)
+        return torch.nn.functional.scaled_dot_product_attention(
+            query, key, value, attn_mask=attention_mask, dropout_p=0.0, is_causal=attention_mask is None)
+
+    def extend_topk(self, query, key, block_indices, block_counts):
+        """Per-head lists: structure rows plus the top-k blocks by pooled q.k."""
+        L = query.shape[2]
+        nb = (L + self.block_size - 1) // self.block_size
+        base = block_indices[0] if block_indices.dim() == 3 else block_indices[0, 0]
+        cnt = block_counts[0] if block_counts.dim() == 2 else block_counts[0, 0]
+        bits = bits_from_indices(base, cnt, nb)
+        qm = K.pool_blocks(query, self.block_size)
+        km = K.pool_blocks(key, self.block_size)
+        idx, c, mx, _ = K.topk_extend(qm, km, bits, self.topk_blocks,
+                                      cap=min(nb, block_indices.shape[-1] + self.topk_blocks))
+        return idx, c
+
+    def clear_cache(self):
+        self.mask_builder.clear_cache()
+
+
+def get_cache_stats() -> Dict[str, int]:
+    stats = {
+        "chunk_cache_size": len(_GLOBAL_CHUNK_CACHE),
+        "line_to_token_cache_size": len(_GLOBAL_LINE_TO_TOKEN_CACHE),
+        "mask_cache_size": len(_GLOBAL_MASK_CACHE),
+        "block_mask_cache_size": len(_BLOCK_MASK_CACHE),
+        "sim_edges_cache_size": 0,
+        "sim_vec_cache_size": 0,
+    }
+    stats["total_cached_items"] = sum(stats.values())
+    return stats
+
+
+def print_cache_stats() -> None:
+    s = get_cache_stats()
+    print("\n" + "=" * 60 + "\nCACHE STATISTICS\n" + "=" * 60)
+    for k, v in s.items():
+        print(f"  {k:32s} {v:3d}")
+    print("=" * 60 + "\n")
+
+
+def clear_all_caches() -> None:
+    for c in (_GLOBAL_CHUNK_CACHE, _GLOBAL_LINE_TO_TOKEN_CACHE, _GLOBAL_MASK_CACHE, _BLOCK_MASK_CACHE):
+        c.clear()
+
+
+# Names the reference uses for the same objects.
+StructureAwareSparseAttentionTriton = StructureAwareSparseAttention

@@ -1,0 +1,202 @@
+"""GPU tests of the public, reference-shaped API: the mask builder end to end,
+the attention module, and a patched LLaMA model against the oracle model."""
+
+import numpy as np
+import pytest
+import torch
+
+import _golden as G
+from oracle import attention_oracle as AO
+from oracle import mask_oracle as MO
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda")
+
+
+@pytest.mark.parametrize("case", G.mask_cases())
+def test_builder_from_chunks_bit_exact(cuda, case):
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+    g = G.load(case)
+    mb = StructureAwareMaskBuilder(G.tokenizer(g), **G.params(g))
+    bi, bc, bm = mb.build_block_indices_from_chunks(
+        str(g["code"]), int(g["seq_len"]), cuda, chunks=G.chunks(g), chunk_deps=G.deps(g),
+        import_chunks=set(g["import_chunks"].tolist()), language=str(g["language"]) or None, batch_size=2)
+    np.testing.assert_array_equal(bm.cpu().numpy(), g["block_mask"])
+    want = np.broadcast_to(g["indices_sorted"], (2,) + g["indices_sorted"].shape[1:])
+    np.testing.assert_array_equal(bi.cpu().numpy(), want)
+    np.testing.assert_array_equal(bc.cpu().numpy(), np.broadcast_to(g["block_counts"], bc.shape))
+
+
+def test_build_block_indices_with_segmenter_bit_exact(cuda):
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder, clear_all_caches
+    from sabrecoder_b200.spans import LineTokenizer
+    g = G.load("builder_full.npz")
+    seg_chunks = G.chunks(g)
+    edges = list(zip(g["edge_src"].tolist(), g["edge_dst"].tolist()))
+
+    class Seg:
+        def __init__(self, tokenizer=None):
+            pass
+
+        def segment_code(self, code, language=None):
+            return list(seg_chunks)
+
+    class Ref:
+        def __init__(self, s, t):
+            self.source_chunk_idx, self.target_chunk_idx = s, t
+
+    class Ana:
+        def __init__(self, chunks, code, language=None):
+            pass
+
+        def analyze(self):
+            return [Ref(a, b) for a, b in edges]
+
+    clear_all_caches()
+    mb = StructureAwareMaskBuilder(LineTokenizer(), segmenter_factory=Seg, analyzer_factory=Ana, **G.params(g))
+    bi, bc, bm = mb.build_block_indices(str(g["code"]), int(g["seq_len"]), cuda, batch_size=2)
+    np.testing.assert_array_equal(bm.cpu().numpy(), g["block_mask"])
+    np.testing.assert_array_equal(bi.cpu().numpy(), g["indices_sorted"])
+    np.testing.assert_array_equal(bc.cpu().numpy(), g["block_counts"])
+
+
+def test_compute_block_indices_from_mask(cuda):
+    from sabrecoder_b200.sabrecoder_attention import compute_block_indices_from_mask
+    g = G.load("mask_c3_16384.npz")
+    m = torch.from_numpy(g["block_mask"].astype(np.int32)).unsqueeze(0)
+    bi, bc = compute_block_indices_from_mask(m.cuda())
+    np.testing.assert_array_equal(bi.cpu().numpy(), g["indices_sorted"])
+    np.testing.assert_array_equal(bc.cpu().numpy(), g["block_counts"])
+    bi2, bc2 = compute_block_indices_from_mask(m)  # CPU tensors come back on the CPU
+    assert bi2.device.type == "cpu"
+    np.testing.assert_array_equal(bi2.numpy(), g["indices_sorted"])
+
+
+@pytest.mark.parametrize("topk", [0, 4])
+def test_sparse_attention_module(cuda, topk):
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareSparseAttention
+    from sabrecoder_b200.sabrecoder_llama import clear_precomputed_blocks, set_precomputed_blocks
+    from sabrecoder_b200.spans import make_spans
+    gen = torch.Generator().manual_seed(11)
+    B, H, L, D, block = 1, 4, 1500, 128, 64
+    q, k, v = (torch.randn(B, L, H, D, generator=gen).to(torch.bfloat16).transpose(1, 2) for _ in range(3))
+    attn = StructureAwareSparseAttention(None, block_size=block, window_size=192, num_prefix_tokens=64,
+                                         num_suffix_tokens=128, global_last_k_chunks=0, max_chunk_tokens=128,
+                                         topk_blocks=topk)
+    bi, bc, bm = attn.mask_builder.build_block_indices_from_spans(make_spans(L, 4), cuda)
+    set_precomputed_blocks(bi, bc)
+    try:
+        out = attn(q.cuda(), k.cuda(), v.cuda(), code="<prompt>")
+    finally:
+        clear_precomputed_blocks()
+    torch.cuda.synchronize()
+    base = bm.cpu().numpy().astype(bool)
+    if topk:
+        qm = MO.pooled_block_means(q.float().numpy(), L, block)
+        km = MO.pooled_block_means(k.float().numpy(), L, block)
+        base = MO.topk_extend_mask(base, MO.pooled_scores(qm, km), topk)
+    ri, rc = MO.block_indices_from_mask(base if base.ndim == 4 else base[None])
+    ref = AO.sparse_prefill_fp32(q, k, v, torch.from_numpy(ri), torch.from_numpy(rc), block)
+    d = (out.float().cpu() - ref).abs()
+    assert d.max().item() <= 2e-2 and d.mean().item() <= 2e-3
+
+
+def _tiny_llama(H, Hkv, layers=2, vocab=512, init=0.08, seed=0):
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(seed)
+    cfg = LlamaConfig(vocab_size=vocab, hidden_size=H * 128, intermediate_size=2 * H * 128,
+                      num_hidden_layers=layers, num_attention_heads=H, num_key_value_heads=Hkv, head_dim=128,
+                      max_position_embeddings=8192, rope_theta=100000.0,
+                      rope_scaling={"rope_type": "linear", "factor": 4.0}, initializer_range=init,
+                      attn_implementation="sdpa")
+    return LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+
+
+@pytest.mark.parametrize("H,Hkv", [(2, 2), (4, 2)])
+def test_patched_llama_prefill_and_greedy_tokens_match_oracle(cuda, H, Hkv):
+    import copy
+
+    from oracle.llama_oracle import patch_oracle
+    from sabrecoder_b200 import sabrecoder_llama as SL
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+    from sabrecoder_b200.spans import make_spans
+    L, block, steps = 700, 64, 32
+    model = _tiny_llama(H, Hkv)
+    # The oracle model runs on the host with the same bf16 weights in the
+    # model's dtype (attention itself in fp32, rounded to bf16 like the kernel).
+    # Both LM heads run in fp32 so that rounding the logits to bf16 (8-bit
+    # mantissa) cannot turn a near-tie into an exact tie.
+    for m in (model,):
+        m.lm_head.float()
+        m.lm_head.register_forward_pre_hook(lambda mod, args: (args[0].float(),))
+    ref_model = copy.deepcopy(model)
+    SL.patch_model_with_sabrecoder_attention(model, None, block_size=block, window_size=192, num_prefix_tokens=64,
+                                             num_suffix_tokens=128, global_last_k_chunks=0, max_chunk_tokens=128,
+                                             verbose=False)
+    model = model.to(cuda)
+    mb = StructureAwareMaskBuilder(None, block_size=block, window_size=192, num_prefix_tokens=64,
+                                   num_suffix_tokens=128, global_last_k_chunks=0, max_chunk_tokens=128)
+    bi, bc, bm = mb.build_block_indices_from_spans(make_spans(L, 8), cuda)
+    patch_oracle(ref_model, bi.cpu(), bc.cpu(), block)
+    ids = torch.randint(0, 512, (1, L), generator=torch.Generator().manual_seed(1))
+    SL.set_current_code("<prompt>")
+    SL.set_precomputed_blocks(bi, bc)
+    try:
+        with torch.no_grad():
+            logits = model(input_ids=ids.to(cuda), logits_to_keep=1).logits.float().cpu()
+            ref_logits = ref_model(input_ids=ids, logits_to_keep=1).logits.float()
+            assert (logits - ref_logits).abs().max().item() < 0.1 * ref_logits.abs().max().item()
+            gen_kw = dict(max_new_tokens=steps, do_sample=False, min_new_tokens=steps, pad_token_id=0,
+                          output_scores=True, return_dict_in_generate=True)
+            out = model.generate(input_ids=ids.to(cuda), **gen_kw)
+            ref_out = ref_model.generate(input_ids=ids, **gen_kw)
+    finally:
+        SL.clear_current_code()
+        SL.clear_precomputed_blocks()
+    got = out.sequences[0, L:].cpu().tolist()
+    want = ref_out.sequences[0, L:].tolist()
+    if got != want:
+        step = next(i for i, (a, b) in enumerate(zip(got, want)) if a != b)
+        rs = ref_out.scores[step][0].float()
+        os_ = out.scores[step][0].float().cpu()
+        top2 = rs.topk(2)
+        raise AssertionError(
+            f"first divergence at step {step}: oracle top-2 {top2.indices.tolist()} margin "
+            f"{(top2.values[0] - top2.values[1]).item():.4f}; ours picks {got[step]} with logits "
+            f"{os_[top2.indices].tolist()}; max logit diff at that step {(os_ - rs).abs().max().item():.4f}")
+
+
+def test_sparse_decode_mode_matches_oracle(cuda):
+    """use_sparse_for_generation: one decode step over the last prompt row's
+    blocks plus the generated blocks."""
+    from sabrecoder_b200 import sabrecoder_llama as SL
+    gen = torch.Generator().manual_seed(2)
+    B, H, D, block, Lp = 1, 4, 128, 64, 1000
+    T = Lp + 70
+    g = G.load("mask_ragged_1000.npz")
+    bi = torch.from_numpy(g["indices_sorted"]).cuda()
+    bc = torch.from_numpy(g["block_counts"]).cuda()
+    SL.set_precomputed_blocks(bi, bc)
+    try:
+        lst, cnt = SL.decode_block_lists(Lp, T, block, cuda)
+    finally:
+        SL.clear_precomputed_blocks()
+    nbp = (Lp + block - 1) // block
+    last = g["indices_sorted"][0, nbp - 1, : g["block_counts"][0, nbp - 1]].tolist()
+    want = last + list(range(nbp, (T + block - 1) // block))
+    assert lst[0, : int(cnt[0])].cpu().tolist() == want
+    q = torch.randn(B, H, D, generator=gen).to(torch.bfloat16)
+    kc = torch.randn(B, H, T, D, generator=gen).to(torch.bfloat16)
+    vc = torch.randn(B, H, T, D, generator=gen).to(torch.bfloat16)
+    from sabrecoder_b200 import kernels as K
+    seq = torch.tensor([T], dtype=torch.int32)
+    out = K.decode_bsa(q.cuda(), kc.cuda(), vc.cuda(), lst, cnt, seq.cuda(), block)
+    ref = AO.sparse_decode_fp32(q, kc, vc, lst.cpu(), cnt.cpu(), seq, block)
+    d = (out.float().cpu() - ref).abs()
+    assert d.max().item() <= 2e-2 and d.mean().item() <= 2e-3
