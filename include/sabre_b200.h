@@ -102,6 +102,29 @@ int sabre_decode_bsa(const void* q, const void* k_cache, const void* v_cache, vo
                      size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * (2b) Split-K decode that allocates nothing and takes no workspace.
+ *
+ * No counterpart in the reference. For callers that cannot provide device
+ * memory at decode time (a runtime that reserves all device memory up front
+ * and rejects later allocations, a foreign-language binding without access
+ * to a caching allocator, a decode loop that must not synchronise on a
+ * cudaMalloc). Same arguments and results as sabre_decode_bsa without the
+ * workspace: the split partials live in a 2 MiB array compiled into the
+ * library (held by every GPU that loads it until exit). Shapes whose
+ * batch * heads_q * (head_dim + 2) floats exceed it are rejected with
+ * SABRE_ERR_UNSUPPORTED. All calls share that array, so calls that overlap
+ * on the GPU race. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make it before
+ * any stream capture.
+ * ---------------------------------------------------------------------- */
+int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o,
+                             const int32_t* block_indices, const int32_t* block_counts, const int32_t* seq_lens,
+                             int batch, int heads_q, int heads_kv, int max_seq, int head_dim, int block_size,
+                             int max_active, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, const int64_t* o_strides, const int64_t* idx_strides,
+                             const int64_t* cnt_strides, float softmax_scale, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * (3) Block-mask construction from token-level structure.
  *
  * Replaces `StructureAwareMaskBuilder._build_block_mask_from_chunks`

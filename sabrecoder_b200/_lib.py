@@ -29,6 +29,8 @@ SIGNATURES = {
     "sabre_decode_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "sabre_decode_bsa": (c_int, [P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                  I64P, I64P, I64P, I64P, I64P, I64P, c_float, c_int, P, c_size_t, P]),
+    "sabre_decode_bsa_noalloc": (c_int, [P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                         I64P, I64P, I64P, I64P, I64P, I64P, c_float, c_int, P]),
     "sabre_block_mask_workspace_size": (c_size_t, [c_int, c_int]),
     "sabre_build_block_mask": (c_int, [P, P, P, c_int, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                        P, P, P, c_size_t, P]),

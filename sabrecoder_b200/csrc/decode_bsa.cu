@@ -351,3 +351,154 @@ int sabre_decode_bsa(const void* q, const void* k_cache, const void* v_cache, vo
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode.
+//
+// Some callers cannot hand this library a workspace: a serving runtime that
+// reserves all device memory at start-up and rejects any later allocation,
+// a foreign-language binding with no access to the framework's caching
+// allocator, or a latency-critical decode loop where a cudaMalloc would
+// synchronise the device. sabre_decode_bsa_noalloc keeps the split partials
+// in a fixed array compiled into this library instead.
+//
+// The array is kNoAllocScratchFloats floats (2 MiB); every GPU that loads the
+// library holds it until the process exits. One decode call needs
+// batch * heads_q * splits * (head_dim + 2) floats; the entry point lowers the
+// split count to fit and rejects shapes that do not fit even with one split.
+// All calls share the array: calls whose kernels overlap on the GPU (on
+// different streams, or on other host threads) race on it. Each call's split
+// kernel writes every partial it later reads, so nothing needs clearing
+// between calls.
+//
+// Host code cannot pass the array's name to a kernel (in host code it names a
+// host-side stand-in, not device memory), so the device address is looked up
+// with cudaGetSymbolAddress once per device, on the first call made while that
+// device is current; make that first call before any stream capture.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace sabre {
+namespace decode {
+
+constexpr size_t kNoAllocScratchFloats = 512u * 1024u;  // 2 MiB
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+static float* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {nullptr};
+static std::mutex g_noalloc_mutex;
+
+static int noalloc_scratch_address(float** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return sabre_cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_decode_bsa_noalloc: device ordinal %d >= %d", dev,
+                      kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return sabre_cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_noalloc_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return SABRE_OK;
+}
+
+}  // namespace decode
+}  // namespace sabre
+
+extern "C" {
+
+int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o,
+                             const int32_t* block_indices, const int32_t* block_counts, const int32_t* seq_lens,
+                             int batch, int heads_q, int heads_kv, int max_seq, int head_dim, int block_size,
+                             int max_active, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, const int64_t* o_strides, const int64_t* idx_strides,
+                             const int64_t* cnt_strides, float softmax_scale, int dtype, void* stream) {
+  using namespace sabre::decode;
+  if (!q || !k_cache || !v_cache || !o || !block_indices || !block_counts || !seq_lens || !q_strides ||
+      !k_strides || !v_strides || !o_strides || !idx_strides || !cnt_strides)
+    return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_decode_bsa_noalloc: null pointer argument");
+  if (batch <= 0 || heads_q <= 0 || heads_kv <= 0 || max_seq <= 0 || max_active <= 0 || block_size <= 0)
+    return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_decode_bsa_noalloc: sizes must be positive");
+  if (heads_q % heads_kv != 0 || heads_q / heads_kv > 8)
+    return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_decode_bsa_noalloc: heads_q/heads_kv must be an integer <= 8");
+  if (head_dim != kD)
+    return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_decode_bsa_noalloc: head_dim %d (only 128)", head_dim);
+  if (dtype != SABRE_BF16 && dtype != SABRE_F16)
+    return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_decode_bsa_noalloc: dtype %d", dtype);
+  if (q_strides[2] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || o_strides[2] != 1)
+    return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_decode_bsa_noalloc: head_dim stride must be 1");
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  if (!al16(q) || !al16(k_cache) || !al16(v_cache))
+    return sabre_fail(SABRE_ERR_ALIGNMENT, "sabre_decode_bsa_noalloc: q/k_cache/v_cache must be 16-byte aligned");
+  const int64_t ss[8] = {q_strides[0], q_strides[1], k_strides[0], k_strides[1],
+                         k_strides[2], v_strides[0], v_strides[1], v_strides[2]};
+  for (int i = 0; i < 8; ++i)
+    if ((ss[i] * 2) % 16 != 0)
+      return sabre_fail(SABRE_ERR_ALIGNMENT, "sabre_decode_bsa_noalloc: q/k/v strides must be 16-byte multiples");
+
+  // Fit the split partials into the fixed array.
+  const size_t per_split = static_cast<size_t>(batch) * heads_q * (static_cast<size_t>(kD) + 2);
+  const size_t max_splits_fit = kNoAllocScratchFloats / per_split;
+  if (max_splits_fit < 1)
+    return sabre_fail(SABRE_ERR_UNSUPPORTED,
+                      "sabre_decode_bsa_noalloc: batch*heads_q = %lld needs %zu floats of scratch per split; the "
+                      "built-in scratch holds %zu floats (2 MiB); use sabre_decode_bsa with a workspace",
+                      static_cast<long long>(batch) * heads_q, per_split, kNoAllocScratchFloats);
+  float* scratch = nullptr;
+  int st = noalloc_scratch_address(&scratch);
+  if (st != SABRE_OK) return st;
+
+  Params p;
+  p.q = q;
+  p.kc = k_cache;
+  p.vc = v_cache;
+  p.o = o;
+  p.idx = block_indices;
+  p.cnt = block_counts;
+  p.seq_lens = seq_lens;
+  p.q_sb = q_strides[0];
+  p.q_sh = q_strides[1];
+  p.k_sb = k_strides[0];
+  p.k_sh = k_strides[1];
+  p.k_st = k_strides[2];
+  p.v_sb = v_strides[0];
+  p.v_sh = v_strides[1];
+  p.v_st = v_strides[2];
+  p.o_sb = o_strides[0];
+  p.o_sh = o_strides[1];
+  p.idx_sb = idx_strides[0];
+  p.idx_sh = idx_strides[1];
+  p.idx_sk = idx_strides[2];
+  p.cnt_sb = cnt_strides[0];
+  p.cnt_sh = cnt_strides[1];
+  p.B = batch;
+  p.Hq = heads_q;
+  p.Hkv = heads_kv;
+  p.Tmax = max_seq;
+  p.block = block_size;
+  p.max_active = max_active;
+  int splits = choose_splits(batch, heads_kv, max_active);
+  if (static_cast<size_t>(splits) > max_splits_fit) splits = static_cast<int>(max_splits_fit);
+  p.splits = splits;
+  p.bps = (max_active + p.splits - 1) / p.splits;
+  const size_t nslots = static_cast<size_t>(batch) * heads_q * p.splits;
+  p.part_acc = scratch;
+  p.part_ml = scratch + nslots * kD;
+  const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(head_dim));
+  p.scale_log2 = scale * 1.4426950408889634f;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int g = heads_q / heads_kv;
+  if (dtype == SABRE_BF16)
+    launch_decode<__nv_bfloat16>(p, g, s);
+  else
+    launch_decode<__half>(p, g, s);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return sabre_cuda_fail(e, "sabre_decode_bsa_noalloc launch");
+  return SABRE_OK;
+}
+
+}  // extern "C"
