@@ -125,6 +125,31 @@ int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_c
                              const int64_t* cnt_strides, float softmax_scale, int dtype, void* stream);
 
 /* ------------------------------------------------------------------------
+ * (1b) Fused rotary embedding + KV store + per-block pooling.
+ *
+ * Replaces apply_rotary_pos_emb and the KV-cache update of the reference
+ * wrapper (methods/sabrecoder/sabrecoder_llama_triton.py:292-299) with one
+ * pass: q_out = rope(q), k_out[pos0 + l] = rope(k), v_out[pos0 + l] = v, with
+ * rope(x) = x*cos + rotate_half(x)*sin rounded per operation in the storage
+ * dtype (bit-identical to transformers' apply_rotary_pos_emb).
+ *
+ * q, k, v  : [B, L, H*, D] strides {b, l, h} (d-stride 1)
+ * cos, sin : [B, L, D] strides {b, l} (the model's position embeddings)
+ * q_out    : [B, L, Hq, D] strides {b, l, h} (may alias q)
+ * k_out, v_out : [B, Hkv, T, D] strides {b, h, t}; rows pos0 .. pos0+L-1
+ * q_pool, k_pool (optional, fp32, contiguous [B, Hq|Hkv, ceil(L/pool_block), D]):
+ *            per-block means of the rotated rows (rows summed first to
+ *            last, then divided by the row count); require pos0 == 0.
+ * head_dim must be 128; strides even, pointers 4-byte aligned.
+ * ---------------------------------------------------------------------- */
+int sabre_rope_qkv(const void* q, const void* k, const void* v, const void* cos, const void* sin, void* q_out,
+                   void* k_out, void* v_out, float* q_pool, float* k_pool, int batch, int seq_len, int heads_q,
+                   int heads_kv, int head_dim, int pool_block, int pos0, const int64_t* q_strides,
+                   const int64_t* k_strides, const int64_t* v_strides, const int64_t* cos_strides,
+                   const int64_t* q_out_strides, const int64_t* k_out_strides, const int64_t* v_out_strides,
+                   int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * (3) Block-mask construction from token-level structure.
  *
  * Replaces `StructureAwareMaskBuilder._build_block_mask_from_chunks`
@@ -185,12 +210,16 @@ int sabre_indices_from_dense(const int32_t* mask, int rows, int ncols, int64_t m
  *   in order d = 0..D-1), ties to the lower kb; write the merged rows as
  *   ascending index lists int32 [B, Hq, nb, cap] + counts [B, Hq, nb] and
  *   max_active_out. Optional out_bits uint32 [B, Hq, nb, nwords].
+ *   workspace: >= sabre_topk_workspace_size(B, Hq, nb) bytes (the fp32
+ *   score matrix). nb <= 1024, topk <= 32, head_dim <= 256.
  * ---------------------------------------------------------------------- */
 int sabre_pool_blocks(const void* x, int batch, int heads, int seq_len, int head_dim, int block_size,
                       const int64_t* x_strides, int dtype, float* out, void* stream);
+size_t sabre_topk_workspace_size(int batch, int heads_q, int num_blocks);
 int sabre_topk_extend(const float* q_pooled, const float* k_pooled, const uint32_t* base_bits, int batch,
                       int heads_q, int heads_kv, int num_blocks, int head_dim, int topk, int32_t* indices,
-                      int cap, int32_t* counts, int32_t* max_active_out, uint32_t* out_bits, void* stream);
+                      int cap, int32_t* counts, int32_t* max_active_out, uint32_t* out_bits, void* workspace,
+                      size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -31,13 +31,17 @@ SIGNATURES = {
                                  I64P, I64P, I64P, I64P, I64P, I64P, c_float, c_int, P, c_size_t, P]),
     "sabre_decode_bsa_noalloc": (c_int, [P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                          I64P, I64P, I64P, I64P, I64P, I64P, c_float, c_int, P]),
+    "sabre_rope_qkv": (c_int, [P, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                               I64P, I64P, I64P, I64P, I64P, I64P, I64P, c_int, P]),
     "sabre_block_mask_workspace_size": (c_size_t, [c_int, c_int]),
     "sabre_build_block_mask": (c_int, [P, P, P, c_int, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                        P, P, P, c_size_t, P]),
     "sabre_indices_from_bits": (c_int, [P, c_int, c_int, P, c_int, P, P, P]),
     "sabre_indices_from_dense": (c_int, [P, c_int, c_int, c_int64, P, c_int, P, P, P]),
     "sabre_pool_blocks": (c_int, [P, c_int, c_int, c_int, c_int, c_int, I64P, c_int, P, P]),
-    "sabre_topk_extend": (c_int, [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, c_int, P, P, P, P]),
+    "sabre_topk_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "sabre_topk_extend": (c_int, [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, c_int, P, P, P, P,
+                                  c_size_t, P]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

@@ -252,96 +252,6 @@ __global__ void pool_blocks_kernel(const T* x, int B, int H, int L, int D, int b
   out[gid] = __fdiv_rn(s, static_cast<float>(n));
 }
 
-constexpr int kTopkMax = 32;
-constexpr int kTopkMaxBlocks = 1024;
-constexpr int kCandPerLane = kTopkMaxBlocks / 32;
-
-// One warp per (b, h, qb). Scores are computed one candidate per lane with
-// a sequential d loop so the rounding order is fixed.
-__global__ void topk_extend_kernel(const float* qm, const float* km, const uint32_t* base_bits, int B, int Hq,
-                                   int Hkv, int nb, int D, int topk, int32_t* idx, int cap, int32_t* counts,
-                                   int32_t* max_active, uint32_t* out_bits) {
-  extern __shared__ float qrow_smem[];
-  const int wib = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + wib;
-  const long long rows = static_cast<long long>(B) * Hq * nb;
-  if (row >= rows) return;
-  const unsigned full = 0xffffffffu;
-  const int qb = static_cast<int>(row % nb);
-  const long long bh = row / nb;
-  const int h = static_cast<int>(bh % Hq);
-  const int b = static_cast<int>(bh / Hq);
-  const int hk = h / (Hq / Hkv);
-  const int nwords = (nb + 31) / 32;
-  float* qrow = qrow_smem + wib * D;
-  const float* qsrc = qm + row * D;
-  for (int d = lane; d < D; d += 32) qrow[d] = qsrc[d];
-  __syncwarp();
-  const float* kbase = km + (static_cast<long long>(b) * Hkv + hk) * nb * D;
-  const uint32_t* brow = base_bits + static_cast<long long>(qb) * nwords;
-
-  // Candidates: kb = lane + 32*i, kb <= qb, not already in the base row.
-  float sc[kCandPerLane];
-  uint32_t candmask = 0u;  // bit i: slot i is a live candidate
-#pragma unroll
-  for (int i = 0; i < kCandPerLane; ++i) {
-    const int kb = lane + 32 * i;
-    sc[i] = 0.f;
-    if (kb <= qb && kb < nb) {
-      const bool in_base = (brow[kb >> 5] >> (kb & 31)) & 1u;
-      if (!in_base) {
-        const float* krow = kbase + static_cast<long long>(kb) * D;
-        float acc = 0.f;
-        for (int d = 0; d < D; ++d) acc = __fadd_rn(acc, __fmul_rn(qrow[d], krow[d]));
-        sc[i] = acc;
-        candmask |= 1u << i;
-      }
-    }
-  }
-  // topk rounds of warp arg-max: larger score first, then smaller kb.
-  uint32_t chosen[kMaxWordsPerLane] = {0u, 0u, 0u, 0u};
-  for (int round = 0; round < topk; ++round) {
-    float best = 0.f;
-    int bkb = -1;
-#pragma unroll
-    for (int i = 0; i < kCandPerLane; ++i) {
-      if ((candmask >> i) & 1u) {
-        const int kb = lane + 32 * i;
-        if (bkb < 0 || sc[i] > best) {  // ascending kb within a lane: strict > keeps the lower kb on ties
-          best = sc[i];
-          bkb = kb;
-        }
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ob = __shfl_xor_sync(full, best, off);
-      const int okb = __shfl_xor_sync(full, bkb, off);
-      const bool take = (okb >= 0) && (bkb < 0 || ob > best || (ob == best && okb < bkb));
-      if (take) {
-        best = ob;
-        bkb = okb;
-      }
-    }
-    if (bkb < 0) break;
-    if ((bkb & 31) == lane) candmask &= ~(1u << (bkb >> 5));
-    // word (bkb >> 5) is owned by lane (bkb >> 5) & 31, slot (bkb >> 10)
-    const int w = bkb >> 5;
-#pragma unroll
-    for (int u = 0; u < kMaxWordsPerLane; ++u)
-      if (lane + 32 * u == w) chosen[u] |= 1u << (bkb & 31);
-  }
-  uint32_t r[kMaxWordsPerLane];
-#pragma unroll
-  for (int u = 0; u < kMaxWordsPerLane; ++u) {
-    const int w = lane + 32 * u;
-    r[u] = (w < nwords) ? (brow[w] | chosen[u]) : 0u;
-    if (out_bits && w < nwords) out_bits[row * nwords + w] = r[u];
-  }
-  emit_row(r, nwords, idx + row * cap, cap, counts + row, max_active);
-}
-
 }  // namespace mask
 }  // namespace sabre
 
@@ -467,33 +377,6 @@ int sabre_pool_blocks(const void* x, int batch, int heads, int seq_len, int head
     return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_pool_blocks: dtype %d", dtype);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return sabre_cuda_fail(e, "sabre_pool_blocks launch");
-  return SABRE_OK;
-}
-
-int sabre_topk_extend(const float* q_pooled, const float* k_pooled, const uint32_t* base_bits, int batch,
-                      int heads_q, int heads_kv, int num_blocks, int head_dim, int topk, int32_t* indices, int cap,
-                      int32_t* counts, int32_t* max_active_out, uint32_t* out_bits, void* stream) {
-  using namespace sabre::mask;
-  if (!q_pooled || !k_pooled || !base_bits || !indices || !counts || !max_active_out || batch <= 0 ||
-      heads_q <= 0 || heads_kv <= 0 || num_blocks <= 0 || head_dim <= 0 || cap <= 0 || topk < 0)
-    return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_topk_extend: bad arguments");
-  if (heads_q % heads_kv != 0)
-    return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_topk_extend: heads_q not a multiple of heads_kv");
-  if (num_blocks > kTopkMaxBlocks || topk > kTopkMax)
-    return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_topk_extend: num_blocks %d (max %d) or topk %d (max %d)",
-                      num_blocks, kTopkMaxBlocks, topk, kTopkMax);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(max_active_out, 0, sizeof(int32_t), s);
-  if (e != cudaSuccess) return sabre_cuda_fail(e, "cudaMemsetAsync(max_active)");
-  const long long rows = static_cast<long long>(batch) * heads_q * num_blocks;
-  const int warps_per_block = 4;
-  const unsigned grid = static_cast<unsigned>((rows + warps_per_block - 1) / warps_per_block);
-  const size_t smem = static_cast<size_t>(warps_per_block) * head_dim * sizeof(float);
-  topk_extend_kernel<<<grid, warps_per_block * 32, smem, s>>>(q_pooled, k_pooled, base_bits, batch, heads_q,
-                                                              heads_kv, num_blocks, head_dim, topk, indices, cap,
-                                                              counts, max_active_out, out_bits);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return sabre_cuda_fail(e, "sabre_topk_extend launch");
   return SABRE_OK;
 }
 

@@ -12,6 +12,8 @@
 #include "prefill_bsa.cu"
 #include "decode_bsa.cu"
 #include "block_mask.cu"
+#include "rope_cache.cu"
+#include "topk.cu"
 
 #define SABRE_VERSION 100
 

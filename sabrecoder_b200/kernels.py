@@ -103,6 +103,47 @@ def prefill_bsa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_indices
     return out
 
 
+def rope_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+             k_out: torch.Tensor, v_out: torch.Tensor, *, q_out: Optional[torch.Tensor] = None, pos0: int = 0,
+             pool_block: int = 0):
+    """Rotary embedding of q and k plus the K/V store, in one pass.
+
+    q, k, v: ``[B, L, H*, D]`` (unit head-dim stride); cos, sin: ``[B, L, D]``;
+    k_out, v_out: ``[B, Hkv, T, D]`` receiving rows ``pos0 .. pos0+L-1``;
+    q_out defaults to q (rotated in place). With ``pool_block > 0`` also
+    returns fp32 per-block means of the rotated q and k
+    (``[B, Hq, nb, D]``, ``[B, Hkv, nb, D]``). Returns ``(q_out, q_pool, k_pool)``."""
+    _need_cuda(q=q, k=k, v=v, cos=cos, sin=sin, k_out=k_out, v_out=v_out)
+    if q.dtype not in DTYPE_CODE or any(t.dtype != q.dtype for t in (k, v, cos, sin, k_out, v_out)):
+        raise SabreError("rope_qkv: q/k/v/cos/sin/k_out/v_out must share dtype bf16 or f16")
+    B, L, Hq, D = q.shape
+    Hkv = k.shape[2]
+    if q_out is None:
+        q_out = q
+    if cos.dim() == 2:
+        cos = cos.unsqueeze(0).expand(B, -1, -1)
+        sin = sin.unsqueeze(0).expand(B, -1, -1)
+    if cos.stride(-1) != 1 or sin.stride() != cos.stride():
+        cos, sin = cos.contiguous(), sin.contiguous()
+    qp = kp = None
+    if pool_block > 0:
+        nb = (L + pool_block - 1) // pool_block
+        qp = torch.empty(B, Hq, nb, D, dtype=torch.float32, device=q.device)
+        kp = torch.empty(B, Hkv, nb, D, dtype=torch.float32, device=q.device)
+
+    def s3(t):
+        return i64((t.stride(0), t.stride(1), t.stride(2)))
+
+    st = lib().sabre_rope_qkv(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(), q_out.data_ptr(),
+        k_out.data_ptr(), v_out.data_ptr(), _ptr(qp), _ptr(kp), B, L, Hq, Hkv, D, int(pool_block), int(pos0),
+        s3(q), s3(k), s3(v), i64((cos.stride(0), cos.stride(1))), s3(q_out), s3(k_out), s3(v_out),
+        DTYPE_CODE[q.dtype], _stream(q))
+    check(st, "sabre_rope_qkv")
+    LAUNCHES[0] += 1
+    return q_out, qp, kp
+
+
 # ---------------------------------------------------------------------------
 # (2) decode
 # ---------------------------------------------------------------------------
@@ -252,10 +293,13 @@ def topk_extend(q_pooled: torch.Tensor, k_pooled: torch.Tensor, base_bits: torch
     cnt = torch.empty(B, Hq, nb, dtype=torch.int32, device=qp.device)
     mx = torch.empty(1, dtype=torch.int32, device=qp.device)
     ob = torch.empty(B, Hq, nb, bb.shape[-1], dtype=torch.int32, device=qp.device) if want_bits else None
+    ws_bytes = int(lib().sabre_topk_workspace_size(B, Hq, nb))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=qp.device)
     check(lib().sabre_topk_extend(qp.data_ptr(), kp.data_ptr(), bb.data_ptr(), B, Hq, Hkv, nb, D, int(topk),
-                                  idx.data_ptr(), cap, cnt.data_ptr(), mx.data_ptr(), _ptr(ob), _stream(qp)),
+                                  idx.data_ptr(), cap, cnt.data_ptr(), mx.data_ptr(), _ptr(ob), ws.data_ptr(),
+                                  ws.numel(), _stream(qp)),
           "sabre_topk_extend")
-    LAUNCHES[0] += 1
+    LAUNCHES[0] += 2
     return idx, cnt, mx, ob
 
 

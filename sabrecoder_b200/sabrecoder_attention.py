@@ -459,6 +459,7 @@ class StructureAwareSparseAttention(nn.Module):
         self.num_suffix_tokens = num_suffix_tokens
         self.use_token_level_sparsity = False
         self.topk_blocks = int(topk_blocks)
+        self._bits_cache = None
         self.mask_builder = StructureAwareMaskBuilder(
             tokenizer=tokenizer, block_size=self.block_size, window_size=window_size,
             num_prefix_tokens=num_prefix_tokens, num_suffix_tokens=num_suffix_tokens,
@@ -490,8 +491,8 @@ class StructureAwareSparseAttention(nn.Module):
     def forward(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, code: str = None,
                 attention_mask: Optional[torch.Tensor] = None,
                 precomputed_block_indices: Optional[torch.Tensor] = None,
-                precomputed_block_counts: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None
-                ) -> torch.Tensor:
+                precomputed_block_counts: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                pooled: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
         B, H, Lq, D = query.shape
         Lk = key.shape[2]
         if code is not None and Lq == Lk and Lq > 1:
@@ -500,7 +501,7 @@ class StructureAwareSparseAttention(nn.Module):
             else:
                 bi, bc = self._lookup_blocks(query, code, B)
             if self.topk_blocks > 0:
-                bi, bc = self.extend_topk(query, key, bi, bc)
+                bi, bc = self.extend_topk(query, key, bi, bc, pooled=pooled)
             return K.prefill_bsa(query, key, value, bi, bc, self.block_size, out=out)
         # Dense path for everything else, as the reference does (:2056-2066).
         if attention_mask is not None and attention_mask.shape[-2:] != (Lq, Lk):
@@ -512,15 +513,26 @@ class StructureAwareSparseAttention(nn.Module):
         return torch.nn.functional.scaled_dot_product_attention(
             query, key, value, attn_mask=attention_mask, dropout_p=0.0, is_causal=attention_mask is None)
 
-    def extend_topk(self, query, key, block_indices, block_counts):
-        """Per-head lists: structure rows plus the top-k blocks by pooled q.k."""
+    def extend_topk(self, query, key, block_indices, block_counts, pooled=None):
+        """Per-head lists: structure rows plus the top-k blocks by pooled q.k.
+        ``pooled`` may carry the per-block means already computed (by the fused
+        RoPE kernel); otherwise they are computed here."""
         L = query.shape[2]
         nb = (L + self.block_size - 1) // self.block_size
         base = block_indices[0] if block_indices.dim() == 3 else block_indices[0, 0]
         cnt = block_counts[0] if block_counts.dim() == 2 else block_counts[0, 0]
-        bits = bits_from_indices(base, cnt, nb)
-        qm = K.pool_blocks(query, self.block_size)
-        km = K.pool_blocks(key, self.block_size)
+        # Every layer of a forward sees the same list tensors; their bitset is
+        # built once (the cache holds the tensors, so identity stays valid).
+        c = self._bits_cache
+        if c is None or c[0] is not block_indices or c[1] is not block_counts or c[2] != nb:
+            c = (block_indices, block_counts, nb, bits_from_indices(base, cnt, nb))
+            self._bits_cache = c
+        bits = c[3]
+        if pooled is not None:
+            qm, km = pooled
+        else:
+            qm = K.pool_blocks(query, self.block_size)
+            km = K.pool_blocks(key, self.block_size)
         idx, c, mx, _ = K.topk_extend(qm, km, bits, self.topk_blocks,
                                       cap=min(nb, block_indices.shape[-1] + self.topk_blocks))
         return idx, c

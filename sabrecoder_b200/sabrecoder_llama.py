@@ -29,6 +29,7 @@ import torch
 import torch.nn as nn
 
 from . import kernels as K
+from .kv_cache import SabreKVCache
 from .sabrecoder_attention import StructureAwareSparseAttention
 
 _SPARSE_CALL_COUNT = 0
@@ -144,16 +145,6 @@ def get_sparsity_stats():
     return s
 
 
-def rotate_pos_emb(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """HF-convention rotary embedding on ``[B, L, H, D]`` with cos/sin
-    ``[B, L, D]`` (same arithmetic as transformers' apply_rotary_pos_emb)."""
-    c = cos.unsqueeze(2)
-    s = sin.unsqueeze(2)
-    h = x.shape[-1] // 2
-    rot = torch.cat((-x[..., h:], x[..., :h]), dim=-1)
-    return x * c + rot * s
-
-
 def decode_block_lists(prompt_len: int, total_len: int, block_size: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
     """Key-block list for a decode step at cache length ``total_len``.
 
@@ -243,12 +234,27 @@ class StructureAwareAttentionWrapper(nn.Module):
         k = self.k_proj(hidden_states).view(B, L, -1, D)
         v = self.v_proj(hidden_states).view(B, L, -1, D)
         cos, sin = position_embeddings
-        q = rotate_pos_emb(q, cos, sin)
-        k = rotate_pos_emb(k, cos, sin)
-        qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
-        if cache is not None:
-            kh, vh = cache.update(kh, vh, self.layer_idx, {"sin": sin, "cos": cos, "cache_position": cache_position})
-        Hq = qh.shape[1]
+        Hq, Hkv = q.shape[2], k.shape[2]
+        # One kernel rotates q in place and writes rotated K and V rows into
+        # [B, Hkv, T, D] storage (the cache's own buffers when it is a
+        # SabreKVCache); a fresh prefill also gets the per-block pooled q/k
+        # the top-k extension needs.
+        pool_block = self.block_size if (L > 1 and self.sparse_attn.topk_blocks > 0) else 0
+        if isinstance(cache, SabreKVCache):
+            kbuf, vbuf, pos0 = cache.slots(self.layer_idx, L)
+            _, qp, kp = K.rope_qkv(q, k, v, cos, sin, kbuf, vbuf, pos0=pos0,
+                                   pool_block=pool_block if pos0 == 0 else 0)
+            kh, vh = cache.advance(self.layer_idx, L)
+        else:
+            kn = torch.empty(B, Hkv, L, D, dtype=q.dtype, device=q.device)
+            vn = torch.empty_like(kn)
+            _, qp, kp = K.rope_qkv(q, k, v, cos, sin, kn, vn, pool_block=pool_block)
+            kh, vh = kn, vn
+            if cache is not None:
+                kh, vh = cache.update(kn, vn, self.layer_idx,
+                                      {"sin": sin, "cos": cos, "cache_position": cache_position})
+        qh = q.transpose(1, 2)
+        pooled = (qp, kp) if qp is not None and kh.shape[2] == L else None
         timing = _ATTENTION_TIMING["enabled"]
         if timing:
             torch.cuda.synchronize()
@@ -276,7 +282,8 @@ class StructureAwareAttentionWrapper(nn.Module):
             out = torch.empty(B, L, Hq, D, dtype=q.dtype, device=q.device)
             code = get_current_code()
             if code is not None and kh.shape[2] == L:
-                self.sparse_attn(qh, kh, vh, code=code, attention_mask=attention_mask, out=out.transpose(1, 2))
+                self.sparse_attn(qh, kh, vh, code=code, attention_mask=attention_mask, out=out.transpose(1, 2),
+                                 pooled=pooled)
             else:
                 out.transpose(1, 2).copy_(self.sparse_attn(qh, kh, vh, code=None, attention_mask=attention_mask))
             attn = out.view(B, L, Hq * D)

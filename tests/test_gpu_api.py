@@ -119,22 +119,28 @@ def _tiny_llama(H, Hkv, layers=2, vocab=512, init=0.08, seed=0):
 
 
 @pytest.mark.parametrize("H,Hkv", [(2, 2), (4, 2)])
-def test_patched_llama_prefill_and_greedy_tokens_match_oracle(cuda, H, Hkv):
+def test_patched_llama_greedy_tokens_match_oracle(cuda, H, Hkv):
+    """Sparse prefill + 32 dense decode steps of a patched 2-layer model
+    against the oracle model on the same bf16 weights, in lockstep: both
+    models are fed the oracle's greedy token every step; each step's logits
+    must agree within 3% of the largest logit magnitude (bf16 models differ by
+    GEMM accumulation order and P rounding), and the greedy choices must
+    agree except where the oracle's own top-2 margin is below that same bound
+    (a near-tie that bf16 rounding of either model may flip)."""
     import copy
+
+    from transformers import DynamicCache
 
     from oracle.llama_oracle import patch_oracle
     from sabrecoder_b200 import sabrecoder_llama as SL
     from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
     from sabrecoder_b200.spans import make_spans
-    L, block, steps = 700, 64, 32
+    L, block, steps, rel = 700, 64, 32, 0.03
     model = _tiny_llama(H, Hkv)
-    # The oracle model runs on the host with the same bf16 weights in the
-    # model's dtype (attention itself in fp32, rounded to bf16 like the kernel).
-    # Both LM heads run in fp32 so that rounding the logits to bf16 (8-bit
-    # mantissa) cannot turn a near-tie into an exact tie.
-    for m in (model,):
-        m.lm_head.float()
-        m.lm_head.register_forward_pre_hook(lambda mod, args: (args[0].float(),))
+    # The LM head runs in fp32 in both models so rounding the logits to bf16
+    # cannot turn a near-tie into an exact tie.
+    model.lm_head.float()
+    model.lm_head.register_forward_pre_hook(lambda mod, args: (args[0].float(),))
     ref_model = copy.deepcopy(model)
     SL.patch_model_with_sabrecoder_attention(model, None, block_size=block, window_size=192, num_prefix_tokens=64,
                                              num_suffix_tokens=128, global_last_k_chunks=0, max_chunk_tokens=128,
@@ -147,29 +153,32 @@ def test_patched_llama_prefill_and_greedy_tokens_match_oracle(cuda, H, Hkv):
     ids = torch.randint(0, 512, (1, L), generator=torch.Generator().manual_seed(1))
     SL.set_current_code("<prompt>")
     SL.set_precomputed_blocks(bi, bc)
+    ca, cb = DynamicCache(), DynamicCache()
+    diffs, flips = [], []
     try:
         with torch.no_grad():
-            logits = model(input_ids=ids.to(cuda), logits_to_keep=1).logits.float().cpu()
-            ref_logits = ref_model(input_ids=ids, logits_to_keep=1).logits.float()
-            assert (logits - ref_logits).abs().max().item() < 0.1 * ref_logits.abs().max().item()
-            gen_kw = dict(max_new_tokens=steps, do_sample=False, min_new_tokens=steps, pad_token_id=0,
-                          output_scores=True, return_dict_in_generate=True)
-            out = model.generate(input_ids=ids.to(cuda), **gen_kw)
-            ref_out = ref_model.generate(input_ids=ids, **gen_kw)
+            la = model(input_ids=ids.to(cuda), past_key_values=ca, use_cache=True, logits_to_keep=1).logits
+            lb = ref_model(input_ids=ids, past_key_values=cb, use_cache=True, logits_to_keep=1).logits
+            for step in range(steps + 1):
+                a = la[0, -1].float().cpu()
+                b = lb[0, -1].float()
+                tol = rel * b.abs().max().item()
+                diffs.append(((a - b).abs().max().item(), tol))
+                top2 = b.topk(2)
+                if step == steps:
+                    break
+                ta, tb = int(a.argmax()), int(top2.indices[0])
+                if ta != tb:
+                    flips.append((step, (top2.values[0] - top2.values[1]).item(), tol))
+                tok = torch.tensor([[tb]])
+                la = model(input_ids=tok.to(cuda), past_key_values=ca, use_cache=True).logits
+                lb = ref_model(input_ids=tok, past_key_values=cb, use_cache=True).logits
     finally:
         SL.clear_current_code()
         SL.clear_precomputed_blocks()
-    got = out.sequences[0, L:].cpu().tolist()
-    want = ref_out.sequences[0, L:].tolist()
-    if got != want:
-        step = next(i for i, (a, b) in enumerate(zip(got, want)) if a != b)
-        rs = ref_out.scores[step][0].float()
-        os_ = out.scores[step][0].float().cpu()
-        top2 = rs.topk(2)
-        raise AssertionError(
-            f"first divergence at step {step}: oracle top-2 {top2.indices.tolist()} margin "
-            f"{(top2.values[0] - top2.values[1]).item():.4f}; ours picks {got[step]} with logits "
-            f"{os_[top2.indices].tolist()}; max logit diff at that step {(os_ - rs).abs().max().item():.4f}")
+    assert all(d < t for d, t in diffs), f"(logit error, bound) per step, prefill first: {diffs}"
+    assert all(m < t for _, m, t in flips), f"greedy choice differs at (step, oracle margin, bound): {flips}"
+    assert len(flips) <= 2, f"too many near-tie flips: {flips}"
 
 
 def test_sparse_decode_mode_matches_oracle(cuda):
@@ -200,3 +209,40 @@ def test_sparse_decode_mode_matches_oracle(cuda):
     ref = AO.sparse_decode_fp32(q, kc, vc, lst.cpu(), cnt.cpu(), seq, block)
     d = (out.float().cpu() - ref).abs()
     assert d.max().item() <= 2e-2 and d.mean().item() <= 2e-3
+
+
+@pytest.mark.parametrize("topk", [0, 8])
+def test_sabre_kv_cache_generate_matches_dynamic_cache(cuda, topk):
+    """The preallocated cache (K/V written in place by the fused RoPE kernel)
+    gives the same logits and tokens as transformers' DynamicCache."""
+    from transformers import DynamicCache
+
+    from sabrecoder_b200 import sabrecoder_llama as SL
+    from sabrecoder_b200.kv_cache import SabreKVCache
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+    from sabrecoder_b200.spans import make_spans
+    L, block = 900, 64
+    model = _tiny_llama(4, 2).to(cuda)
+    SL.patch_model_with_sabrecoder_attention(model, None, block_size=block, window_size=192, num_prefix_tokens=64,
+                                             num_suffix_tokens=128, global_last_k_chunks=0, max_chunk_tokens=128,
+                                             topk_blocks=topk, verbose=False)
+    mb = StructureAwareMaskBuilder(None, block_size=block, window_size=192, num_prefix_tokens=64,
+                                   num_suffix_tokens=128, global_last_k_chunks=0, max_chunk_tokens=128)
+    bi, bc, _ = mb.build_block_indices_from_spans(make_spans(L, 3), cuda)
+    ids = torch.randint(0, 512, (1, L), generator=torch.Generator().manual_seed(4)).to(cuda)
+    SL.set_current_code("<prompt>")
+    SL.set_precomputed_blocks(bi, bc)
+    try:
+        with torch.no_grad():
+            kw = dict(max_new_tokens=12, do_sample=False, min_new_tokens=12, pad_token_id=0,
+                      output_scores=True, return_dict_in_generate=True)
+            a = model.generate(input_ids=ids, past_key_values=DynamicCache(), **kw)
+            cache = SabreKVCache(model.config, batch_size=1, max_cache_len=L + 16, device=cuda)
+            b = model.generate(input_ids=ids, past_key_values=cache, **kw)
+    finally:
+        SL.clear_current_code()
+        SL.clear_precomputed_blocks()
+    assert torch.equal(a.sequences, b.sequences)
+    for sa, sb in zip(a.scores, b.scores):
+        assert torch.equal(sa, sb)
+    assert cache.get_seq_length() == L + 11

@@ -238,3 +238,33 @@ def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
 
 def test_no_device_timeouts_recorded(K):
     assert K.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("B,L,Hq,Hkv,pool,dtype", [(1, 1000, 4, 2, 64, torch.bfloat16), (2, 300, 2, 2, 128, torch.bfloat16),
+                                                   (1, 1, 4, 4, 0, torch.bfloat16), (1, 257, 2, 1, 64, torch.float16)])
+def test_rope_qkv_bit_exact_with_hf(K, B, L, Hq, Hkv, pool, dtype):
+    """Fused RoPE + KV store equals transformers' apply_rotary_pos_emb bit for
+    bit; pools equal the oracle's block means of the rotated rows."""
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+    gen = torch.Generator().manual_seed(L + Hq)
+    D = 128
+    qkv = torch.randn(B, L, (Hq + 2 * Hkv) * D, generator=gen).to(dtype)
+    q = qkv[..., : Hq * D].view(B, L, Hq, D)
+    k = qkv[..., Hq * D: (Hq + Hkv) * D].view(B, L, Hkv, D)
+    v = qkv[..., (Hq + Hkv) * D:].view(B, L, Hkv, D)
+    ang = torch.rand(B, L, D // 2, generator=gen) * 50
+    emb = torch.cat([ang, ang], -1)
+    cos, sin = emb.cos().to(dtype), emb.sin().to(dtype)
+    rq, rk = apply_rotary_pos_emb(q.transpose(1, 2), k.transpose(1, 2), cos, sin)
+    T, pos0 = L + 5, 3 if pool == 0 else 0
+    qd = q.cuda().clone()
+    kc = torch.zeros(B, Hkv, T + pos0, D, dtype=dtype, device="cuda")
+    vc = torch.zeros_like(kc)
+    _, qp, kp = K.rope_qkv(qd, k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), kc, vc, pos0=pos0, pool_block=pool)
+    torch.cuda.synchronize()
+    assert torch.equal(qd.transpose(1, 2).cpu(), rq)
+    assert torch.equal(kc[:, :, pos0: pos0 + L].cpu(), rk)
+    assert torch.equal(vc[:, :, pos0: pos0 + L].cpu(), v.transpose(1, 2))
+    if pool:
+        np.testing.assert_array_equal(qp.cpu().numpy(), MO.pooled_block_means(rq.float().numpy(), L, pool))
+        np.testing.assert_array_equal(kp.cpu().numpy(), MO.pooled_block_means(rk.float().numpy(), L, pool))
