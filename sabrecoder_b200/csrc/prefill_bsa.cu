@@ -6,17 +6,20 @@
 // 1/sqrt(D) (:67), P rounded to the input dtype before P.V (:107), fully
 // masked rows output zeros (:112).
 //
-// Design (one CTA = 128 query rows of one head; 192 threads; 2 CTAs per SM):
+// Design (one CTA = 128 query rows of one head; 224 threads; 2 CTAs per SM):
 //   warps 0-3  softmax + epilogue; thread t owns query row t = TMEM lane t
-//   warp 4     TMA producer: Q tile once, then K/V key tiles (64 keys each)
-//              into a 2-stage ring, only for the key tiles that the two
-//              64-row halves of the query tile list
-//   warp 5     TMEM allocator and single-thread tcgen05.mma issuer:
-//              S = Q K^T (M=128, N=64, K=128) into a double-buffered TMEM
-//              S tile, then O += P V (M=128, N=128, K=64) into TMEM O.
-// TMEM: O at columns [0,128), S buffers at [128,192) and [192,256).
-// Shared memory (bytes): Q 32768 | K 2x16384 | V 2x16384 | P 16384 |
-// per-half key-tile bitmaps 256 | barriers | misc  (~112.4 KB).
+//   warp 4     TMA producer for K (3-stage ring, a stage is released as soon
+//              as the S = Q K^T that read it completes)
+//   warp 5     TMEM allocator and single-thread tcgen05.mma issuer
+//   warp 6     TMA producer for V (2-stage ring, released when P.V completes)
+// TMEM (256 columns): O [0,128), S [128,192), P0 [192,224), P1 [224,256).
+//   S = Q K^T      M=128 N=64  K=128, A and B from shared memory
+//   O += P V       M=128 N=128 K=64,  A (P, bf16 pairs) from TMEM, B (V)
+//                  from shared memory (MN-major)
+// Shared memory (bytes): Q 32768 | K 3x16384 | V 2x16384 | key-tile bitmaps
+// 256 | barriers (~112.5 KB). The Q buffer doubles as the staging tile of
+// the epilogue's TMA store of O.
+//
 // The key-tile list of a CTA is the union of the lists of the (one or two)
 // query blocks its rows belong to, kept as two 1024-bit bitmaps (one per
 // 64-row half) so any list order, duplicates and out-of-range entries are
@@ -26,6 +29,8 @@
 // The running max used to scale P is only raised when the row max grows by
 // more than 2^8 (the result is exact: O and l share the same stale max);
 // O in TMEM is then rescaled by the softmax threads between P.V MMAs.
+// All waits are bounded (see common.cuh); on a timeout every role drains
+// what it issued, TMEM is freed and the CTA exits.
 #include "common.cuh"
 
 namespace sabre {
@@ -34,32 +39,43 @@ namespace prefill {
 constexpr int kD = 128;
 constexpr int kTileM = 128;
 constexpr int kTileN = 64;
-constexpr int kStages = 2;
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
 constexpr int kMaxKeyTiles = 1024;  // seq_len <= 65536
 constexpr int kWords = kMaxKeyTiles / 32;
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;
 
-constexpr int kQBytes = kTileM * kD * 2;         // 32768
-constexpr int kKVStageBytes = kTileN * kD * 2;   // 16384 (two 8 KB d-halves)
+constexpr int kQBytes = kTileM * kD * 2;        // 32768
+constexpr int kKVStageBytes = kTileN * kD * 2;  // 16384 (two 8 KB d-halves)
 constexpr int kQOff = 0;
 constexpr int kKOff = kQOff + kQBytes;
-constexpr int kVOff = kKOff + kStages * kKVStageBytes;
-constexpr int kPOff = kVOff + kStages * kKVStageBytes;
-constexpr int kBitsOff = kPOff + kTileM * kTileN * 2;
+constexpr int kVOff = kKOff + kKStages * kKVStageBytes;
+constexpr int kBitsOff = kVOff + kVStages * kKVStageBytes;
 constexpr int kBarOff = kBitsOff + 2 * kWords * 4;
-enum Bar { Q_FULL = 0, KV_FULL = 1, KV_EMPTY = 3, S_FULL = 5, S_EMPTY = 7, P_FULL = 9, P_EMPTY = 10, MMA_DONE = 11,
-           NUM_BARS = 12 };
+enum Bar {
+  Q_FULL = 0,
+  K_FULL = 1,                     // [3]
+  K_EMPTY = K_FULL + kKStages,    // [3]
+  V_FULL = K_EMPTY + kKStages,    // [2]
+  V_EMPTY = V_FULL + kVStages,    // [2]
+  S_FULL = V_EMPTY + kVStages,
+  S_EMPTY = S_FULL + 1,
+  P_FULL = S_EMPTY + 1,           // [2]
+  P_EMPTY = P_FULL + 2,           // [2]
+  MMA_DONE = P_EMPTY + 2,
+  NUM_BARS = MMA_DONE + 1
+};
 constexpr int kMiscOff = kBarOff + NUM_BARS * 8;
 constexpr int kSmemBytes = kMiscOff + 16;
 constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemS = 128;
+constexpr uint32_t kTmemP = 192;  // + 32 * buffer
 
 struct Params {
   const int32_t* idx;
   const int32_t* cnt;
-  void* o;
   long long idx_sb, idx_sh, idx_sm, idx_sk;
   long long cnt_sb, cnt_sh, cnt_sm;
-  long long o_sb, o_sh, o_sl;
   int B, Hq, Hkv, L, block, max_active, ntiles, nkt;
   float scale_log2;
 };
@@ -87,7 +103,8 @@ struct UnionIter {
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_bsa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, const Params p) {
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                       const Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -114,19 +131,26 @@ __global__ void __launch_bounds__(kThreads, 2)
   for (int i = tid; i < 2 * kWords; i += kThreads) bits[i] = 0u;
   if (warp == 4 && lane == 0) {
     mbar_init(bar(Q_FULL), 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(KV_FULL + s), 1);
-      mbar_init(bar(KV_EMPTY + s), 1);
-      mbar_init(bar(S_FULL + s), 1);
-      mbar_init(bar(S_EMPTY + s), 128);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(bar(K_FULL + s), 1);
+      mbar_init(bar(K_EMPTY + s), 1);
     }
-    mbar_init(bar(P_FULL), 128);
-    mbar_init(bar(P_EMPTY), 1);
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(bar(V_FULL + s), 1);
+      mbar_init(bar(V_EMPTY + s), 1);
+    }
+    mbar_init(bar(S_FULL), 1);
+    mbar_init(bar(S_EMPTY), 128);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(P_FULL + s), 128);
+      mbar_init(bar(P_EMPTY + s), 1);
+    }
     mbar_init(bar(MMA_DONE), 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmO);
   }
   if (warp == 5) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -167,68 +191,72 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr uint32_t kIdescQK = idesc_f16(128, 64, DT<T>::kBf16, false);
   constexpr uint32_t kIdescPV = idesc_f16(128, 128, DT<T>::kBf16, true);
 
-  if (warp == 4) {
-    // ---------------- TMA producer ----------------
+  if (warp == 4 || warp == 6) {
+    // ---------------- TMA producers (warp 4: Q and K, warp 6: V) ----------------
     if (lane == 0 && start_ok) {
-      int issued[kStages] = {0, 0};
-      mbar_arrive_expect_tx(bar(Q_FULL), kQBytes);
-      tma_load_4d(sbase + kQOff, &tmQ, bar(Q_FULL), 0, r0, h, b);
-      tma_load_4d(sbase + kQOff + kQBytes / 2, &tmQ, bar(Q_FULL), 64, r0, h, b);
+      const bool is_k = (warp == 4);
+      const int stages = is_k ? kKStages : kVStages;
+      const int full0 = is_k ? K_FULL : V_FULL;
+      const int empty0 = is_k ? K_EMPTY : V_EMPTY;
+      const uint32_t ring = sbase + (is_k ? kKOff : kVOff);
+      const CUtensorMap* map = is_k ? &tmK : &tmV;
+      int issued[kKStages] = {0, 0, 0};
+      if (is_k) {
+        mbar_arrive_expect_tx(bar(Q_FULL), kQBytes);
+        tma_load_4d(sbase + kQOff, &tmQ, bar(Q_FULL), 0, r0, h, b);
+        tma_load_4d(sbase + kQOff + kQBytes / 2, &tmQ, bar(Q_FULL), 64, r0, h, b);
+      }
       UnionIter it(bits, bits + kWords, nw);
       for (int j = 0;; ++j) {
         const int kt = it.next();
         if (kt < 0) break;
-        const int s = j & 1;
-        if (!mbar_wait(bar(KV_EMPTY + s), ((j >> 1) & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(bar(KV_FULL + s), 2 * kKVStageBytes);
-        const uint32_t kd = sbase + kKOff + s * kKVStageBytes;
-        const uint32_t vd = sbase + kVOff + s * kKVStageBytes;
-        tma_load_4d(kd, &tmK, bar(KV_FULL + s), 0, kt * 64, hk, b);
-        tma_load_4d(kd + kKVStageBytes / 2, &tmK, bar(KV_FULL + s), 64, kt * 64, hk, b);
-        tma_load_4d(vd, &tmV, bar(KV_FULL + s), 0, kt * 64, hk, b);
-        tma_load_4d(vd + kKVStageBytes / 2, &tmV, bar(KV_FULL + s), 64, kt * 64, hk, b);
+        const int s = j % stages;
+        if (!mbar_wait(bar(empty0 + s), ((j / stages) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(bar(full0 + s), kKVStageBytes);
+        const uint32_t dst = ring + s * kKVStageBytes;
+        tma_load_4d(dst, map, bar(full0 + s), 0, kt * 64, hk, b);
+        tma_load_4d(dst + kKVStageBytes / 2, map, bar(full0 + s), 64, kt * 64, hk, b);
         ++issued[s];
       }
       // Every issued copy must land before the CTA may exit.
-      mbar_wait_drain(bar(Q_FULL), 0);
-      for (int s = 0; s < kStages; ++s)
-        if (issued[s] > 0) mbar_wait_drain(bar(KV_FULL + s), (issued[s] - 1) & 1);
+      if (is_k) mbar_wait_drain(bar(Q_FULL), 0);
+      for (int s = 0; s < stages; ++s)
+        if (issued[s] > 0) mbar_wait_drain(bar(full0 + s), (issued[s] - 1) & 1);
     }
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && start_ok) {
       const uint32_t qa = sbase + kQOff;
-      const uint32_t pa = sbase + kPOff;
       bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag);
-      auto issue_pv = [&](int j1) -> bool {
-        const int s1 = j1 & 1;
-        if (!mbar_wait(bar(P_FULL), j1 & 1, abort_flag)) return false;
+      auto issue_pv = [&](int i) -> bool {
+        const int pb = i & 1;
+        if (!mbar_wait(bar(P_FULL + pb), (i >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait(bar(V_FULL + pb), (i >> 1) & 1, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t va = sbase + kVOff + s1 * kKVStageBytes;
+        const uint32_t va = sbase + kVOff + pb * kKVStageBytes;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = smem_desc_sw128(pa + kk * 32, 16, 1024);
           const uint64_t bd = smem_desc_sw128(va + kk * 2048, kKVStageBytes / 2, 1024);
-          mma_f16_ss(tmem, ad, bd, kIdescPV, (j1 > 0 || kk > 0) ? 1u : 0u);
+          mma_f16_ts(tmem, tmem + kTmemP + 32 * pb + 8 * kk, bd, kIdescPV, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(bar(KV_EMPTY + s1));
-        mma_commit(bar(P_EMPTY));
+        mma_commit(bar(P_EMPTY + pb));
+        mma_commit(bar(V_EMPTY + pb));
         return true;
       };
       for (int j = 0; ok && j < n; ++j) {
-        const int s = j & 1;
-        const int ph = (j >> 1) & 1;
-        if (!mbar_wait(bar(KV_FULL + s), ph, abort_flag)) { ok = false; break; }
-        if (!mbar_wait(bar(S_EMPTY + s), ph ^ 1, abort_flag)) { ok = false; break; }
+        const int ks = j % kKStages;
+        if (!mbar_wait(bar(K_FULL + ks), (j / kKStages) & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(bar(S_EMPTY), (j & 1) ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t ka = sbase + kKOff + s * kKVStageBytes;
+        const uint32_t ka = sbase + kKOff + ks * kKVStageBytes;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t ad = smem_desc_sw128(qa + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = smem_desc_sw128(ka + (kk >> 2) * (kKVStageBytes / 2) + (kk & 3) * 32, 16, 1024);
-          mma_f16_ss(tmem + 128 + 64 * s, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
+          mma_f16_ss(tmem + kTmemS, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar(S_FULL + s));
+        mma_commit(bar(S_FULL));
+        mma_commit(bar(K_EMPTY + ks));
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok && n >= 1) issue_pv(n - 1);
@@ -249,17 +277,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     UnionIter it(bits, bits + kWords, nw);
     for (int j = 0; ok && j < n; ++j) {
       const int kt = it.next();
-      const int s = j & 1;
-      ok = mbar_wait(bar(S_FULL + s), (j >> 1) & 1, abort_flag);
+      ok = mbar_wait(bar(S_FULL), j & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       uint32_t sr0[32], sr1[32];
-      tmem_ld32(tl + 128 + 64 * s, sr0);
-      tmem_ld32(tl + 128 + 64 * s + 32, sr1);
+      tmem_ld32(tl + kTmemS, sr0);
+      tmem_ld32(tl + kTmemS + 32, sr1);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(bar(S_EMPTY + s));
+      mbar_arrive(bar(S_EMPTY));
 
       const bool vis = (bits[half * kWords + (kt >> 5)] >> (kt & 31)) & 1u;
       const int nvalid = vis ? min(64, max(0, r_abs - kt * 64 + 1)) : 0;
@@ -294,45 +321,50 @@ __global__ void __launch_bounds__(kThreads, 2)
       l_run = l_run * alpha + rs;
       m_run = m_use;
 
-      // P.V of the previous key tile must be done before P is overwritten
-      // and before O is rescaled.
-      if (j >= 1) {
-        ok = mbar_wait(bar(P_EMPTY), (j - 1) & 1, abort_flag);
+      // O must not change under a running P.V: rescale only after P.V(j-1).
+      if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
+        const int pb1 = (j - 1) & 1;
+        ok = mbar_wait(bar(P_EMPTY + pb1), ((j - 1) >> 1) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-          for (int ch = 0; ch < 4; ++ch) {
-            uint32_t ov[32];
-            tmem_ld32(tl + ch * 32, ov);
-            tmem_wait_ld();
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t ov[32];
+          tmem_ld32(tl + ch * 32, ov);
+          tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
-            tmem_st32(tl + ch * 32, ov);
-          }
-          tmem_wait_st();
+          for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+          tmem_st32(tl + ch * 32, ov);
         }
+        tmem_wait_st();
       }
-      uint8_t* prow = smem + kPOff + row * 128;
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        *reinterpret_cast<uint4*>(prow + ((c8 ^ (row & 7)) << 4)) =
-            make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
-      }
-      fence_proxy_async_smem();
+      // P buffer j&1 was last read by P.V(j-2).
+      const int pb = j & 1;
+      ok = mbar_wait(bar(P_EMPTY + pb), ((j >> 1) & 1) ^ 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      tmem_st32(tl + kTmemP + 32 * pb, pk);
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(P_FULL));
+      mbar_arrive(bar(P_FULL + pb));
     }
-    // Epilogue: O / l -> global, one row per thread.
+    // Epilogue: O / l, staged as a swizzled [128][64] x 2 tile in the Q buffer
+    // (free once the last P.V completed) and written by a TMA store.
     if (ok && n >= 1) {
-      ok = mbar_wait(bar(P_EMPTY), (n - 1) & 1, abort_flag);
+      ok = mbar_wait(bar(P_EMPTY + ((n - 1) & 1)), ((n - 1) >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
+    } else if (ok) {
+      // No key tile: nothing consumed Q, so its load may still be landing in
+      // the buffer the output is staged in.
+      ok = mbar_wait(bar(Q_FULL), 0, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
     }
+    ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       const float inv = (l_run > 0.f) ? 1.0f / l_run : 0.0f;
-      T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh + static_cast<long long>(r_abs) * p.o_sl;
 #pragma unroll 1
       for (int ch = 0; ch < 4; ++ch) {
         uint32_t ov[32];
@@ -343,17 +375,28 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int c = 0; c < 32; ++c) ov[c] = 0u;
         }
-        if (r_abs < p.L) {
-          uint32_t pkd[16];
+        uint32_t pkd[16];
 #pragma unroll
-          for (int c = 0; c < 32; c += 2)
-            pkd[c >> 1] = DT<T>::pack(__uint_as_float(ov[c]) * inv, __uint_as_float(ov[c + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
+        for (int c = 0; c < 32; c += 2)
+          pkd[c >> 1] = DT<T>::pack(__uint_as_float(ov[c]) * inv, __uint_as_float(ov[c + 1]) * inv);
+        // columns [32ch, 32ch+32) = d-half ch/2, 16-byte chunks 4*(ch&1) .. +3
+        uint8_t* rowp = smem + kQOff + (ch >> 1) * (kQBytes / 2) + row * 128;
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-            dst[q4] = make_uint4(pkd[4 * q4], pkd[4 * q4 + 1], pkd[4 * q4 + 2], pkd[4 * q4 + 3]);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int chunk = 4 * (ch & 1) + q4;
+          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) =
+              make_uint4(pkd[4 * q4], pkd[4 * q4 + 1], pkd[4 * q4 + 2], pkd[4 * q4 + 3]);
         }
       }
+      fence_proxy_async_smem();
+    }
+    named_bar_sync(1, 128);
+    // After a timeout anywhere in the CTA the tile is incomplete: skip the store.
+    if (tid == 0 && start_ok && *abort_flag == 0) {
+      tma_store_4d(&tmO, sbase + kQOff, 0, r0, h, b);
+      tma_store_4d(&tmO, sbase + kQOff + kQBytes / 2, 64, r0, h, b);
+      tma_store_commit();
+      tma_store_wait_read();
     }
   }
 

@@ -157,8 +157,11 @@ int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, cons
     if ((o_strides[i] * 2) % 16 != 0)
       return fail(SABRE_ERR_ALIGNMENT, "sabre_prefill_bsa: o stride %d not a 16-byte multiple", i);
 
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   int st;
+  if ((st = make_map_bhld(&mo, o, dtype, batch, heads_q, seq_len, head_dim, o_strides[0], o_strides[1],
+                          o_strides[2], kTileM, "o")) != SABRE_OK)
+    return st;
   if ((st = make_map_bhld(&mq, q, dtype, batch, heads_q, seq_len, head_dim, q_strides[0], q_strides[1],
                           q_strides[2], kTileM, "q")) != SABRE_OK)
     return st;
@@ -172,7 +175,6 @@ int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, cons
   Params p;
   p.idx = block_indices;
   p.cnt = block_counts;
-  p.o = o;
   p.idx_sb = idx_strides[0];
   p.idx_sh = idx_strides[1];
   p.idx_sm = idx_strides[2];
@@ -180,9 +182,6 @@ int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, cons
   p.cnt_sb = cnt_strides[0];
   p.cnt_sh = cnt_strides[1];
   p.cnt_sm = cnt_strides[2];
-  p.o_sb = o_strides[0];
-  p.o_sh = o_strides[1];
-  p.o_sl = o_strides[2];
   p.B = batch;
   p.Hq = heads_q;
   p.Hkv = heads_kv;
@@ -200,10 +199,10 @@ int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, cons
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SABRE_BF16) {
     if ((st = ensure_smem_attr(prefill_bsa_kernel<__nv_bfloat16>, kSmemBytes)) != SABRE_OK) return st;
-    prefill_bsa_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
+    prefill_bsa_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, mo, p);
   } else {
     if ((st = ensure_smem_attr(prefill_bsa_kernel<__half>, kSmemBytes)) != SABRE_OK) return st;
-    prefill_bsa_kernel<__half><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
+    prefill_bsa_kernel<__half><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, mo, p);
   }
   SABRE_CUDA_TRY(cudaGetLastError());
   return SABRE_OK;

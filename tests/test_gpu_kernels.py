@@ -102,6 +102,25 @@ def test_prefill_ignores_invalid_entries(K):
     _close(out, ref)
 
 
+def test_prefill_empty_lists_give_zero_rows(K):
+    """Query blocks with count 0 attend to nothing and output zeros (the
+    reference divides by l = 1 when l == 0, :112); a whole 128-row tile with
+    empty lists is covered too."""
+    gen = torch.Generator().manual_seed(9)
+    B, H, L, D, block = 1, 2, 640, 128, 64
+    q, k, v = (torch.randn(B, H, L, D, generator=gen).to(torch.bfloat16) for _ in range(3))
+    nb = L // block
+    bi, bc = _random_lists(B, nb, gen)
+    bc[0, 2] = 0
+    bc[0, 3] = 0  # query blocks 2 and 3 form one 128-row tile
+    bc[0, 7] = 0
+    out = K.prefill_bsa(q.cuda(), k.cuda(), v.cuda(), bi.cuda(), bc.cuda(), block)
+    torch.cuda.synchronize()
+    ref = AO.sparse_prefill_fp32(q, k, v, bi, bc, block)
+    _close(out, ref)
+    assert out[:, :, 128:256].abs().max().item() == 0.0
+
+
 def test_prefill_config0_shape(K):
     """B=1, H=16, L=4096, D=128, block 64 with a structure mask + top-8."""
     gen = torch.Generator().manual_seed(0)
