@@ -140,9 +140,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(bar(V_EMPTY + s), 1);
     }
     mbar_init(bar(S_FULL), 1);
-    mbar_init(bar(S_EMPTY), 128);
+    mbar_init(bar(S_EMPTY), 4);  // one arrival per softmax warp
     for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(P_FULL + s), 128);
+      mbar_init(bar(P_FULL + s), 4);
       mbar_init(bar(P_EMPTY + s), 1);
     }
     mbar_init(bar(MMA_DONE), 1);
@@ -226,19 +226,26 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && start_ok) {
-      const uint32_t qa = sbase + kQOff;
+      // This thread shares its SM sub-partition with softmax warps that want
+      // every issue slot, so its path is kept short: all shared-memory
+      // descriptors are built once and stepped by adding constants to the
+      // start-address field (units of 16 bytes; no carry out of the field).
+      const uint64_t qd = smem_desc_sw128(sbase + kQOff, 16, 1024);
+      const uint64_t kd0 = smem_desc_sw128(sbase + kKOff, 16, 1024);
+      const uint64_t vd0 = smem_desc_sw128(sbase + kVOff, kKVStageBytes / 2, 1024);
+      const uint32_t s_tmem = tmem + kTmemS;
+      const uint32_t p_tmem = tmem + kTmemP;
       bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag);
       auto issue_pv = [&](int i) -> bool {
         const int pb = i & 1;
         if (!mbar_wait(bar(P_FULL + pb), (i >> 1) & 1, abort_flag)) return false;
         if (!mbar_wait(bar(V_FULL + pb), (i >> 1) & 1, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t va = sbase + kVOff + pb * kKVStageBytes;
+        const uint64_t vd = vd0 + static_cast<uint64_t>(pb * (kKVStageBytes >> 4));
+        const uint32_t pa = p_tmem + 32 * pb;
+        mma_f16_ts(tmem, pa, vd, kIdescPV, i > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t bd = smem_desc_sw128(va + kk * 2048, kKVStageBytes / 2, 1024);
-          mma_f16_ts(tmem, tmem + kTmemP + 32 * pb + 8 * kk, bd, kIdescPV, (i > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 1; kk < 4; ++kk) mma_f16_ts(tmem, pa + 8 * kk, vd + kk * (2048 >> 4), kIdescPV, 1u);
         mma_commit(bar(P_EMPTY + pb));
         mma_commit(bar(V_EMPTY + pb));
         return true;
@@ -248,12 +255,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!mbar_wait(bar(K_FULL + ks), (j / kKStages) & 1, abort_flag)) { ok = false; break; }
         if (!mbar_wait(bar(S_EMPTY), (j & 1) ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t ka = sbase + kKOff + ks * kKVStageBytes;
+        const uint64_t kd = kd0 + static_cast<uint64_t>(ks * (kKVStageBytes >> 4));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = smem_desc_sw128(qa + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(ka + (kk >> 2) * (kKVStageBytes / 2) + (kk & 3) * 32, 16, 1024);
-          mma_f16_ss(tmem + kTmemS, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
+          const uint64_t qo = ((kk >> 2) * (kQBytes / 2) + (kk & 3) * 32) >> 4;
+          const uint64_t ko = ((kk >> 2) * (kKVStageBytes / 2) + (kk & 3) * 32) >> 4;
+          mma_f16_ss(s_tmem, qd + qo, kd + ko, kIdescQK, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar(S_FULL));
         mma_commit(bar(K_EMPTY + ks));
@@ -277,8 +284,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     UnionIter it(bits, bits + kWords, nw);
     for (int j = 0; ok && j < n; ++j) {
       const int kt = it.next();
-      ok = mbar_wait(bar(S_FULL), j & 1, abort_flag);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = mbar_wait_warp(bar(S_FULL), j & 1, abort_flag);
       if (!ok) break;
       tc_fence_after();
       uint32_t sr0[32], sr1[32];
@@ -286,7 +292,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       tmem_ld32(tl + kTmemS + 32, sr1);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(bar(S_EMPTY));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(S_EMPTY));
 
       const bool vis = (bits[half * kWords + (kt >> 5)] >> (kt & 31)) & 1u;
       const int nvalid = vis ? min(64, max(0, r_abs - kt * 64 + 1)) : 0;
@@ -301,31 +308,36 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < 64; ++c)
           if (c >= nvalid) x[c] = -INFINITY;
       }
-      float mx = x[0];
+      // Row max as 8 independent chains, then a tree (short dependency chain).
+      float m8[8];
 #pragma unroll
-      for (int c = 1; c < 64; ++c) mx = fmaxf(mx, x[c]);
+      for (int i = 0; i < 8; ++i) m8[i] = x[i];
+#pragma unroll
+      for (int c = 8; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], x[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       const float m_tile = mx * sl2;
       const bool rescale = m_tile > m_run + 8.0f;
       const float m_use = rescale ? m_tile : m_run;
       const float alpha = rescale ? ex2(m_run - m_use) : 1.0f;
       const float moff = (m_use == -INFINITY) ? 0.0f : m_use;
-      float rs = 0.f;
+      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 64; c += 2) {
         const float p0 = ex2(fmaf(x[c], sl2, -moff));
         const float p1 = ex2(fmaf(x[c + 1], sl2, -moff));
-        rs += p0 + p1;
+        s8[(c >> 1) & 7] += p0 + p1;
         pk[c >> 1] = DT<T>::pack(p0, p1);
       }
+      const float rs = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
       l_run = l_run * alpha + rs;
       m_run = m_use;
 
       // O must not change under a running P.V: rescale only after P.V(j-1).
       if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
         const int pb1 = (j - 1) & 1;
-        ok = mbar_wait(bar(P_EMPTY + pb1), ((j - 1) >> 1) & 1, abort_flag);
-        ok = __all_sync(0xffffffffu, ok);
+        ok = mbar_wait_warp(bar(P_EMPTY + pb1), ((j - 1) >> 1) & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll 1
@@ -341,14 +353,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       // P buffer j&1 was last read by P.V(j-2).
       const int pb = j & 1;
-      ok = mbar_wait(bar(P_EMPTY + pb), ((j >> 1) & 1) ^ 1, abort_flag);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = mbar_wait_warp(bar(P_EMPTY + pb), ((j >> 1) & 1) ^ 1, abort_flag);
       if (!ok) break;
       tc_fence_after();
       tmem_st32(tl + kTmemP + 32 * pb, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(P_FULL + pb));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(P_FULL + pb));
     }
     // Epilogue: O / l, staged as a swizzled [128][64] x 2 tile in the Q buffer
     // (free once the last P.V completed) and written by a TMA store.
