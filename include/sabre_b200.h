@@ -140,7 +140,7 @@ int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_c
  * q_pool, k_pool (optional, fp32, contiguous [B, Hq|Hkv, ceil(L/pool_block), D]):
  *            per-block means of the rotated rows (rows summed first to
  *            last, then divided by the row count); require pos0 == 0.
- * head_dim must be 128; strides even, pointers 4-byte aligned.
+ * head_dim must be 128; strides multiples of 8 elements, pointers 16-byte aligned.
  * ---------------------------------------------------------------------- */
 int sabre_rope_qkv(const void* q, const void* k, const void* v, const void* cos, const void* sin, void* q_out,
                    void* k_out, void* v_out, float* q_pool, float* k_pool, int batch, int seq_len, int heads_q,

@@ -14,10 +14,13 @@
 // fp32, then divided by the row count -- the same order sabre_pool_blocks
 // uses).
 //
-// Layout: one warp owns one head for a block of rows and walks the rows in
-// order; lane l handles d = {2l, 2l+1} and their rotation partners
-// {2l+64, 2l+65}, so a warp reads and writes each 256-byte row as two
-// 128-byte segments.
+// Layout: a CTA owns a block of rows (the pool block, or 64 rows) for 16
+// heads; its 4 warps take 4 heads each, 8 lanes per head. Lane c of a head
+// group holds d = [8c, 8c+8) and the rotation partners [64+8c, 64+8c+8) as
+// two 16-byte vectors, so the four heads of a warp read one contiguous 1 KB
+// span of a [B, L, H, D] row. Each lane walks its rows in order (which keeps
+// the pooled sums in row order) with kU rows of loads in flight. cos/sin rows
+// are staged once per 64-row chunk in shared memory and shared by all heads.
 #include "common.cuh"
 
 namespace sabre {
@@ -25,7 +28,10 @@ namespace rope {
 
 constexpr int kD = 128;
 constexpr int kWarps = 4;
-constexpr int kUnroll = 4;
+constexpr int kHeadsPerWarp = 4;
+constexpr int kHeadsPerCta = kWarps * kHeadsPerWarp;
+constexpr int kChunk = 64;  // rows of cos/sin staged at a time
+constexpr int kU = 4;       // rows of q/k/v loads in flight per lane
 
 struct Params {
   const void* q;
@@ -49,123 +55,152 @@ struct Params {
 };
 
 template <typename T>
-__device__ __forceinline__ float2 ld2(const T* p) {
-  const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
-  if constexpr (DT<T>::kBf16) {
-    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
-  } else {
-    return __half22float2(*reinterpret_cast<const __half2*>(&u));
-  }
-}
-
-template <typename T>
 __device__ __forceinline__ float rnd(float x) {
   return DT<T>::to_f(DT<T>::from_f(x));
 }
 
+// 8 packed 16-bit values <-> 8 floats.
 template <typename T>
-__device__ __forceinline__ void st2(T* p, float a, float b) {
-  *reinterpret_cast<uint32_t*>(p) = DT<T>::pack(a, b);
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (DT<T>::kBf16) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    } else {
+      const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kWarps * 32) rope_qkv_kernel(const Params p) {
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int head = blockIdx.y * kWarps + warp;  // 0..Hq+2*Hkv-1
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(DT<T>::pack(f[0], f[1]), DT<T>::pack(f[2], f[3]), DT<T>::pack(f[4], f[5]),
+                    DT<T>::pack(f[6], f[7]));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32, 4) rope_qkv_kernel(const Params p) {
+  __shared__ uint4 s_cos[kChunk][kD / 8];
+  __shared__ uint4 s_sin[kChunk][kD / 8];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int c = lane & 7;
+  const int head = blockIdx.y * kHeadsPerCta + warp * kHeadsPerWarp + (lane >> 3);
   const int b = blockIdx.z;
   const int r0 = blockIdx.x * p.rows;
   const int r1 = min(r0 + p.rows, p.L);
   const int nheads = p.Hq + 2 * p.Hkv;
-  if (head >= nheads || r0 >= p.L) return;
+  const bool active = head < nheads;
   const int kind = head < p.Hq ? 0 : (head < p.Hq + p.Hkv ? 1 : 2);
   const int h = kind == 0 ? head : (kind == 1 ? head - p.Hq : head - p.Hq - p.Hkv);
-  const int d0 = 2 * lane;
 
-  const T* src;
-  long long s_l;
-  T* dst;
-  long long d_row, d_base;
+  const T* src = nullptr;
+  long long s_l = 0, d_row = 0, d_base = 0;
+  T* dst = nullptr;
   float* pool = nullptr;
-  if (kind == 0) {
-    src = static_cast<const T*>(p.q) + b * p.q_sb + h * p.q_sh;
-    s_l = p.q_sl;
-    dst = static_cast<T*>(p.q_out);
-    d_base = b * p.qo_sb + h * p.qo_sh;
-    d_row = p.qo_sl;
-    if (p.q_pool) pool = p.q_pool + ((static_cast<long long>(b) * p.Hq + h) * p.nb) * kD;
-  } else if (kind == 1) {
-    src = static_cast<const T*>(p.k) + b * p.k_sb + h * p.k_sh;
-    s_l = p.k_sl;
-    dst = static_cast<T*>(p.k_out);
-    d_base = b * p.ko_sb + h * p.ko_sh + static_cast<long long>(p.pos0) * p.ko_st;
-    d_row = p.ko_st;
-    if (p.k_pool) pool = p.k_pool + ((static_cast<long long>(b) * p.Hkv + h) * p.nb) * kD;
-  } else {
-    src = static_cast<const T*>(p.v) + b * p.v_sb + h * p.v_sh;
-    s_l = p.v_sl;
-    dst = static_cast<T*>(p.v_out);
-    d_base = b * p.vo_sb + h * p.vo_sh + static_cast<long long>(p.pos0) * p.vo_st;
-    d_row = p.vo_st;
+  if (active) {
+    if (kind == 0) {
+      src = static_cast<const T*>(p.q) + b * p.q_sb + h * p.q_sh;
+      s_l = p.q_sl;
+      dst = static_cast<T*>(p.q_out);
+      d_base = b * p.qo_sb + h * p.qo_sh;
+      d_row = p.qo_sl;
+      if (p.q_pool) pool = p.q_pool + ((static_cast<long long>(b) * p.Hq + h) * p.nb) * kD;
+    } else if (kind == 1) {
+      src = static_cast<const T*>(p.k) + b * p.k_sb + h * p.k_sh;
+      s_l = p.k_sl;
+      dst = static_cast<T*>(p.k_out);
+      d_base = b * p.ko_sb + h * p.ko_sh + static_cast<long long>(p.pos0) * p.ko_st;
+      d_row = p.ko_st;
+      if (p.k_pool) pool = p.k_pool + ((static_cast<long long>(b) * p.Hkv + h) * p.nb) * kD;
+    } else {
+      src = static_cast<const T*>(p.v) + b * p.v_sb + h * p.v_sh;
+      s_l = p.v_sl;
+      dst = static_cast<T*>(p.v_out);
+      d_base = b * p.vo_sb + h * p.vo_sh + static_cast<long long>(p.pos0) * p.vo_st;
+      d_row = p.vo_st;
+    }
   }
   const T* cbase = static_cast<const T*>(p.cos) + b * p.c_sb;
   const T* sbase = static_cast<const T*>(p.sin) + b * p.c_sb;
 
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int rb = r0; rb < r1; rb += kUnroll) {
-    float2 xl[kUnroll], xh[kUnroll], cl[kUnroll], ch[kUnroll], sl[kUnroll], sh[kUnroll];
+  float acc_lo[8], acc_hi[8];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int r = rb + u;
-      if (r < r1) {
-        const T* xr = src + static_cast<long long>(r) * s_l;
-        xl[u] = ld2(xr + d0);
-        xh[u] = ld2(xr + d0 + 64);
-        if (kind != 2) {
-          const T* cr = cbase + static_cast<long long>(r) * p.c_sl;
-          const T* sr = sbase + static_cast<long long>(r) * p.c_sl;
-          cl[u] = ld2(cr + d0);
-          ch[u] = ld2(cr + d0 + 64);
-          sl[u] = ld2(sr + d0);
-          sh[u] = ld2(sr + d0 + 64);
+  for (int i = 0; i < 8; ++i) acc_lo[i] = acc_hi[i] = 0.f;
+
+  for (int cr0 = r0; cr0 < r1; cr0 += kChunk) {
+    const int cr1 = min(cr0 + kChunk, r1);
+    __syncthreads();  // previous chunk's cos/sin no longer read
+    for (int i = tid; i < (cr1 - cr0) * (kD / 8); i += kWarps * 32) {
+      const int rr = i >> 4, cc = i & 15;
+      const long long off = static_cast<long long>(cr0 + rr) * p.c_sl + cc * 8;
+      s_cos[rr][cc] = *reinterpret_cast<const uint4*>(cbase + off);
+      s_sin[rr][cc] = *reinterpret_cast<const uint4*>(sbase + off);
+    }
+    __syncthreads();
+    if (!active) continue;
+    for (int rb = cr0; rb < cr1; rb += kU) {
+      uint4 xl[kU], xh[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (rb + u < cr1) {
+          const T* xr = src + static_cast<long long>(rb + u) * s_l + 8 * c;
+          xl[u] = *reinterpret_cast<const uint4*>(xr);
+          xh[u] = *reinterpret_cast<const uint4*>(xr + 64);
         }
       }
-    }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int r = rb + u;
-      if (r >= r1) break;
-      float ol0, ol1, oh0, oh1;
-      if (kind == 2) {
-        ol0 = xl[u].x;
-        ol1 = xl[u].y;
-        oh0 = xh[u].x;
-        oh1 = xh[u].y;
-      } else {
-        // d < 64: x[d]*cos[d] + (-x[d+64])*sin[d]; d >= 64: x[d]*cos[d] + x[d-64]*sin[d]
-        ol0 = rnd<T>(rnd<T>(xl[u].x * cl[u].x) + rnd<T>(-xh[u].x * sl[u].x));
-        ol1 = rnd<T>(rnd<T>(xl[u].y * cl[u].y) + rnd<T>(-xh[u].y * sl[u].y));
-        oh0 = rnd<T>(rnd<T>(xh[u].x * ch[u].x) + rnd<T>(xl[u].x * sh[u].x));
-        oh1 = rnd<T>(rnd<T>(xh[u].y * ch[u].y) + rnd<T>(xl[u].y * sh[u].y));
-      }
-      T* dr = dst + d_base + static_cast<long long>(r) * d_row;
-      st2(dr + d0, ol0, ol1);
-      st2(dr + d0 + 64, oh0, oh1);
-      if (pool) {
-        acc[0] = __fadd_rn(acc[0], ol0);
-        acc[1] = __fadd_rn(acc[1], ol1);
-        acc[2] = __fadd_rn(acc[2], oh0);
-        acc[3] = __fadd_rn(acc[3], oh1);
+      for (int u = 0; u < kU; ++u) {
+        const int r = rb + u;
+        if (r >= cr1) break;
+        float a[8], bh[8], ol[8], oh[8];
+        unpack8<T>(xl[u], a);
+        unpack8<T>(xh[u], bh);
+        if (kind == 2) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            ol[i] = a[i];
+            oh[i] = bh[i];
+          }
+        } else {
+          float cl[8], ch[8], sl[8], sh[8];
+          unpack8<T>(s_cos[r - cr0][c], cl);
+          unpack8<T>(s_cos[r - cr0][8 + c], ch);
+          unpack8<T>(s_sin[r - cr0][c], sl);
+          unpack8<T>(s_sin[r - cr0][8 + c], sh);
+          // d < 64: x[d]*cos[d] + (-x[d+64])*sin[d]; d >= 64: x[d]*cos[d] + x[d-64]*sin[d]
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            ol[i] = rnd<T>(rnd<T>(a[i] * cl[i]) + rnd<T>(-bh[i] * sl[i]));
+            oh[i] = rnd<T>(rnd<T>(bh[i] * ch[i]) + rnd<T>(a[i] * sh[i]));
+          }
+        }
+        T* dr = dst + d_base + static_cast<long long>(r) * d_row + 8 * c;
+        *reinterpret_cast<uint4*>(dr) = pack8<T>(ol);
+        *reinterpret_cast<uint4*>(dr + 64) = pack8<T>(oh);
+        if (pool) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            acc_lo[i] = __fadd_rn(acc_lo[i], ol[i]);
+            acc_hi[i] = __fadd_rn(acc_hi[i], oh[i]);
+          }
+        }
       }
     }
   }
   if (pool) {
     const float n = static_cast<float>(r1 - r0);
-    float* pr = pool + static_cast<long long>(blockIdx.x) * kD;
-    pr[d0] = __fdiv_rn(acc[0], n);
-    pr[d0 + 1] = __fdiv_rn(acc[1], n);
-    pr[d0 + 64] = __fdiv_rn(acc[2], n);
-    pr[d0 + 65] = __fdiv_rn(acc[3], n);
+    float* pr = pool + static_cast<long long>(blockIdx.x) * kD + 8 * c;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      pr[i] = __fdiv_rn(acc_lo[i], n);
+      pr[64 + i] = __fdiv_rn(acc_hi[i], n);
+    }
   }
 }
 
@@ -198,12 +233,12 @@ int sabre_rope_qkv(const void* q, const void* k, const void* v, const void* cos,
   const int nst[7] = {3, 3, 3, 2, 3, 3, 3};
   for (int i = 0; i < 7; ++i)
     for (int j = 0; j < nst[i]; ++j)
-      if (all[i][j] % 2 != 0)
-        return sabre_fail(SABRE_ERR_ALIGNMENT, "sabre_rope_qkv: strides must be even (4-byte pair access)");
+      if (all[i][j] % 8 != 0)
+        return sabre_fail(SABRE_ERR_ALIGNMENT, "sabre_rope_qkv: strides must be multiples of 8 elements (16-byte access)");
   const void* ptrs[8] = {q, k, v, cos, sin, q_out, k_out, v_out};
   for (int i = 0; i < 8; ++i)
-    if ((reinterpret_cast<uintptr_t>(ptrs[i]) & 3u) != 0)
-      return sabre_fail(SABRE_ERR_ALIGNMENT, "sabre_rope_qkv: pointers must be 4-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(ptrs[i]) & 15u) != 0)
+      return sabre_fail(SABRE_ERR_ALIGNMENT, "sabre_rope_qkv: pointers must be 16-byte aligned");
   Params p;
   p.q = q;
   p.k = k;
@@ -243,7 +278,7 @@ int sabre_rope_qkv(const void* q, const void* k, const void* v, const void* cos,
   p.rows = (q_pool || k_pool) ? pool_block : 64;
   p.nb = (seq_len + p.rows - 1) / p.rows;
   const int nheads = heads_q + 2 * heads_kv;
-  dim3 grid(p.nb, (nheads + kWarps - 1) / kWarps, batch);
+  dim3 grid(p.nb, (nheads + kHeadsPerCta - 1) / kHeadsPerCta, batch);
   if (grid.y > 65535u || grid.z > 65535u)
     return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_rope_qkv: grid too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
