@@ -62,6 +62,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-only", action="store_true",
                     help="time the prefill attention kernel alone on one layer of the workload")
+    ap.add_argument("--decode-op", choices=["dense", "sparse"], default=None,
+                    help="time the decode attention kernel alone on one layer of the workload: over every cached "
+                         "block (dense) or over the last prompt row's list plus the generated blocks (sparse)")
     return ap.parse_args()
 
 
@@ -294,6 +297,8 @@ def run_ours(args, rank, world, dist):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     arch, prompts, scaling = workload(args.workload, rank, world)
+    if args.decode_op:
+        return run_decode_op(args, rank, world, dist)
     if arch is None or args.attn_only:
         return run_op_bench(args, rank, world, dist)
     model, cfg = build_model(arch, dev)
@@ -483,6 +488,22 @@ def e2e_through_api(model, mb, prepared, args, dev, dist, cache):
     return {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
 
+class L2Flush:
+    """Evicts the 126 MB L2 between timed launches by reading a 256 MB buffer
+    (a sum into one scalar). Reading leaves only clean lines behind, so the
+    timed kernel does not pay for writing back a flush buffer's dirty lines."""
+    NOTE = "L2 flushed between iterations by reading a 256 MB buffer"
+
+    def __init__(self, dev):
+        import torch
+        self.buf = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+        self.out = torch.empty((), dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        import torch
+        torch.sum(self.buf, dim=0, out=self.out)
+
+
 OP_SHAPES = {"c0": (16, 4096, "spans"), "c1": (16, 12288, "bench"), "c2": (16, 16384, "bench"),
              "c3": (32, 16384, "bench")}
 
@@ -509,13 +530,13 @@ def run_op_bench(args, rank, world, dist):
     ma = int(mx.item())
     idx = idx[..., :ma].contiguous()
     out = torch.empty_like(q)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     for _ in range(args.warmup):
         K.prefill_bsa(q, k, v, idx, cnt, blk, out=out)
     torch.cuda.synchronize()
     tot = 0.0
     for _ in range(args.steps):
-        flush.zero_()
+        flush()
         s, e = torch.cuda.Event(True), torch.cuda.Event(True)
         s.record()
         K.prefill_bsa(q, k, v, idx, cnt, blk, out=out)
@@ -535,11 +556,94 @@ def run_op_bench(args, rank, world, dist):
                           "dtype": "bf16", "data": "synthetic",
                           "config": {"workload": f"{args.workload} attention op: B=1 H={H} L={L} D=128 block 64, "
                                                  f"structure + top-{TOPK}, density {dens:.4f}",
-                                     "l2": "L2 flushed (256 MB write) between iterations"},
+                                     "l2": L2Flush.NOTE},
                           "roofline": {"kernel": "sabre prefill_bsa_kernel", "bound": "tensor",
                                        "achieved": flop / ms / 1e9, "peak": burst, "unit": "TFLOP/s",
                                        "frac": flop / ms / 1e9 / burst, "peak_kind": f"{which} bf16 dense, burst",
                                        "flop_per_launch": flop, "ms_per_launch": ms, "traffic": traffic}}))
+
+
+DECODE_SHAPES = {"c0": (16, 4096, 64), "c1": (16, 12288, 64), "c2": (16, 16384, 64), "c3": (32, 16384, 128)}
+
+
+def run_decode_op(args, rank, world, dist):
+    """The decode attention op alone on one layer's shape of the workload: one
+    query row per head after a prompt of L tokens and `gen` generated tokens
+    (c1: H=16, L=12288, 64 generated; c3: H=32, L=16384, 128 generated), K/V
+    cache in HBM, L2 flushed between timed launches. Bytes counted are the K
+    and V rows of the listed blocks (plus q and o)."""
+    import torch
+    from sabrecoder_b200 import kernels as K
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+    from sabrecoder_b200.spans import BENCH_SPAN_MIX, make_spans
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    H, L, gen = DECODE_SHAPES[args.workload]
+    blk = MASK["block_size"]
+    T = L + gen
+    g = torch.Generator(device=dev).manual_seed(rank)
+    kc = torch.randn(1, H, T, 128, device=dev, generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(1, H, T, 128, device=dev, generator=g, dtype=torch.bfloat16)
+    q = torch.randn(1, H, 128, device=dev, generator=g, dtype=torch.bfloat16)
+    nbk = (T + blk - 1) // blk
+    if args.decode_op == "dense":
+        lst = torch.arange(nbk, device=dev, dtype=torch.int32).unsqueeze(0)
+        cnt = torch.tensor([nbk], dtype=torch.int32, device=dev)
+    else:
+        mb = StructureAwareMaskBuilder(None, **MASK)
+        bi, bc, _ = mb.build_block_indices_from_spans(make_spans(L, 1000 + rank, **BENCH_SPAN_MIX), dev)
+        nb_p = (L + blk - 1) // blk
+        c_last = int(bc[0, nb_p - 1].item())
+        lst = torch.cat([bi[0, nb_p - 1, :c_last].to(torch.int32),
+                         torch.arange(nb_p, nbk, device=dev, dtype=torch.int32)]).unsqueeze(0).contiguous()
+        cnt = torch.tensor([lst.shape[1]], dtype=torch.int32, device=dev)
+    seq = torch.tensor([T], dtype=torch.int32, device=dev)
+    ws = torch.empty(K.decode_workspace_bytes(1, H, H, 128, lst.shape[1]), dtype=torch.uint8, device=dev)
+    out = torch.empty_like(q)
+    flush = L2Flush(dev)
+    for _ in range(max(3, args.warmup)):
+        K.decode_bsa(q, kc, vc, lst, cnt, seq, blk, out=out, workspace=ws)
+    torch.cuda.synchronize()
+    # Replayed from a CUDA graph so the host-side argument handling of the
+    # Python call cannot leak into the device-timed window.
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            K.decode_bsa(q, kc, vc, lst, cnt, seq, blk, out=out, workspace=ws)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(args.steps):
+        flush()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        graph.replay()
+        e.record()
+        torch.cuda.synchronize()
+        tot += s.elapsed_time(e)
+    ms = tot / args.steps
+    rows = 0
+    for kb in lst[0, :int(cnt.item())].tolist():
+        rows += max(0, min(blk, T - kb * blk))
+    nbytes = rows * H * 128 * 2 * 2 + 2 * H * 128 * 2
+    gbs = nbytes / ms / 1e6
+    _, _, hbm, which = measured_peaks()
+    traffic = profile_traffic(f"decode_bsa_{args.workload}_{args.decode_op}")
+    if rank == 0:
+        print(json.dumps({"metric": "decode attention GB/s (single op)", "value": gbs, "unit": "GB/s",
+                          "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                          "data": "synthetic",
+                          "config": {"workload": f"{args.workload} decode op: B=1 H={H} cache {T} tokens D=128 "
+                                                 f"block {blk}, {args.decode_op} list of {int(cnt.item())} blocks",
+                                     "l2": L2Flush.NOTE},
+                          "roofline": {"kernel": "sabre decode_split_kernel + decode_combine_kernel",
+                                       "bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                                       "frac": gbs / hbm, "peak_kind": f"{which} HBM copy bandwidth",
+                                       "bytes_per_launch": nbytes, "ms_per_launch": ms, "traffic": traffic}}))
 
 
 def main():

@@ -18,7 +18,7 @@ constexpr int kD = 128;
 constexpr int kThreads = 128;       // 4 warps
 constexpr int kRowsPerHalf = 4;     // rows per half-warp per step
 constexpr int kRowsPerStep = 4 * 2 * kRowsPerHalf;  // 32 rows per CTA step
-constexpr int kTargetCtas = 4 * 148;
+constexpr int kTargetCtas = 2 * 148;
 constexpr int kMaxSplits = 256;
 
 struct Params {
@@ -41,9 +41,10 @@ struct Params {
   float scale_log2;
 };
 
+// Splits per (sequence, KV head): enough CTAs for one wave of two per SM.
 static inline int choose_splits(int batch, int heads_kv, int max_active) {
   long long groups = static_cast<long long>(batch) * heads_kv;
-  int s = static_cast<int>((kTargetCtas + groups - 1) / groups);
+  int s = static_cast<int>(kTargetCtas / groups);
   s = s < 1 ? 1 : s;
   s = s > max_active ? max_active : s;
   return s > kMaxSplits ? kMaxSplits : s;
@@ -219,6 +220,252 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const Params p) 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Streaming variant for caches whose rows are contiguous per head (row stride
+// == head_dim, the layout of a [B, Hkv, T, D] cache): every 64-row chunk of a
+// listed block is one 16 KB span of K and one of V, fetched by a single
+// producer thread with bulk copies into a kBulkStages-deep shared-memory ring
+// (mbarrier completion), while 4 consumer warps score and accumulate from
+// shared memory with the same per-(warp half, head) online softmax as above.
+// ~96 KB of copies in flight per CTA and 2 CTAs per SM cover HBM latency
+// without holding the rows in registers.
+// ---------------------------------------------------------------------------
+constexpr int kBulkStages = 3;
+constexpr int kChunkRows = 64;
+constexpr int kChunkBytes = kChunkRows * kD * 2;  // 16384 per tensor
+constexpr int kBulkConsumerWarps = 4;
+constexpr int kBulkThreads = (kBulkConsumerWarps + 1) * 32;
+constexpr int kBulkRingBytes = kBulkStages * 2 * kChunkBytes;
+constexpr int kBulkBarOff = kBulkRingBytes;
+constexpr int kBulkSmem = kBulkBarOff + 2 * kBulkStages * 8 + 16;
+constexpr int kBulkTargetCtas = 2 * 148;
+
+// Walks the 64-row chunks of a split's share of one list: the same sequence
+// for the producer and the consumers.
+struct ChunkWalk {
+  const int32_t* ip;
+  long long sk;
+  int jj, j1, block, T_valid, kb, sub;
+  __device__ ChunkWalk(const int32_t* ip_, long long sk_, int j0, int j1_, int block_, int T_valid_)
+      : ip(ip_), sk(sk_), jj(j0 - 1), j1(j1_), block(block_), T_valid(T_valid_), kb(0), sub(0) {
+    sub = block_ / kChunkRows;  // forces a fetch on the first next()
+  }
+  // Next chunk: first row t0 and valid rows; false when the share is exhausted.
+  __device__ bool next(long long& t0, int& rows) {
+    for (;;) {
+      if (sub < block / kChunkRows) {
+        const long long t = static_cast<long long>(kb) * block + static_cast<long long>(sub) * kChunkRows;
+        ++sub;
+        if (t < T_valid) {
+          t0 = t;
+          rows = static_cast<int>(min(static_cast<long long>(kChunkRows), T_valid - t));
+          return true;
+        }
+        sub = block / kChunkRows;
+        continue;
+      }
+      if (++jj >= j1) return false;
+      kb = ip[jj * sk];
+      sub = (kb < 0) ? block / kChunkRows : 0;
+    }
+  }
+};
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Params p) {
+  constexpr bool kBf16 = DT<T>::kBf16;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  const int split = blockIdx.x;
+  const int hk = blockIdx.y;
+  const int b = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int g = p.Hq / p.Hkv;
+  const unsigned full = 0xffffffffu;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBulkBarOff + 2 * kBulkStages * 8);
+  auto full_bar = [&](int s) -> uint32_t { return sbase + kBulkBarOff + 8u * s; };
+  auto empty_bar = [&](int s) -> uint32_t { return sbase + kBulkBarOff + 8u * (kBulkStages + s); };
+
+  if (tid == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < kBulkStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), kBulkConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int T_valid = min(p.seq_lens[b], p.Tmax);
+  int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];
+  cnt = min(cnt, p.max_active);
+  const int j0 = split * p.bps;
+  const int j1 = min(j0 + p.bps, cnt);
+  const int32_t* ip = p.idx + b * p.idx_sb + hk * p.idx_sh;
+  const T* kbase = static_cast<const T*>(p.kc) + b * p.k_sb + hk * p.k_sh;
+  const T* vbase = static_cast<const T*>(p.vc) + b * p.v_sb + hk * p.v_sh;
+
+  float m[G], l[G], acc[G][8];
+  if (warp == kBulkConsumerWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      ChunkWalk walk(ip, p.idx_sk, j0, j1, p.block, T_valid);
+      long long t0;
+      int rows;
+      int issued[kBulkStages] = {0, 0, 0};
+      for (int i = 0; walk.next(t0, rows); ++i) {
+        const int s = i % kBulkStages;
+        if (!mbar_wait(empty_bar(s), ((i / kBulkStages) & 1) ^ 1, abort_flag)) break;
+        const uint32_t bytes = static_cast<uint32_t>(rows) * kD * 2;
+        mbar_arrive_expect_tx(full_bar(s), 2 * bytes);
+        const uint32_t dst = sbase + s * 2 * kChunkBytes;
+        bulk_load(dst, kbase + t0 * kD, bytes, full_bar(s));
+        bulk_load(dst + kChunkBytes, vbase + t0 * kD, bytes, full_bar(s));
+        ++issued[s];
+      }
+      // Every issued copy must land before the ring is reused or the CTA exits.
+      for (int s = 0; s < kBulkStages; ++s)
+        if (issued[s] > 0) mbar_wait_drain(full_bar(s), (issued[s] - 1) & 1);
+    }
+  } else {
+    // ---------------- consumers: warp w owns rows [16w, 16w+16) of a chunk ----------------
+    const int half = lane >> 4;
+    const int c = lane & 15;
+    float qv[G][8];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) {
+      if (gi < g) {
+        const T* qp = static_cast<const T*>(p.q) + b * p.q_sb + (hk * g + gi) * p.q_sh + c * 8;
+        const uint4 u = *reinterpret_cast<const uint4*>(qp);
+        unpack8(u, qv[gi], kBf16);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) qv[gi][e] *= p.scale_log2;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) qv[gi][e] = 0.f;
+      }
+      m[gi] = -INFINITY;
+      l[gi] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[gi][e] = 0.f;
+    }
+    ChunkWalk walk(ip, p.idx_sk, j0, j1, p.block, T_valid);
+    long long t0;
+    int rows;
+    for (int i = 0; walk.next(t0, rows); ++i) {
+      const int s = i % kBulkStages;
+      if (!mbar_wait_warp(full_bar(s), (i / kBulkStages) & 1, abort_flag)) break;
+      // The phase is complete; each lane's own probe gives it acquire order on the copied bytes.
+      (void)mbar_test_wait(full_bar(s), (i / kBulkStages) & 1);
+      const uint4* sk = reinterpret_cast<const uint4*>(smem + s * 2 * kChunkBytes);
+      const uint4* sv = reinterpret_cast<const uint4*>(smem + s * 2 * kChunkBytes + kChunkBytes);
+#pragma unroll
+      for (int batch = 0; batch < 2; ++batch) {
+        uint4 kr[kRowsPerHalf], vr[kRowsPerHalf];
+        bool valid[kRowsPerHalf];
+#pragma unroll
+        for (int u = 0; u < kRowsPerHalf; ++u) {
+          const int row = warp * 16 + half * 8 + batch * kRowsPerHalf + u;
+          valid[u] = row < rows;
+          kr[u] = valid[u] ? sk[row * 16 + c] : make_uint4(0u, 0u, 0u, 0u);
+          vr[u] = valid[u] ? sv[row * 16 + c] : make_uint4(0u, 0u, 0u, 0u);
+        }
+        float sc[kRowsPerHalf][G];
+#pragma unroll
+        for (int u = 0; u < kRowsPerHalf; ++u) {
+          float kf[8];
+          unpack8(kr[u], kf, kBf16);
+#pragma unroll
+          for (int gi = 0; gi < G; ++gi) {
+            float d = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) d = fmaf(qv[gi][e], kf[e], d);
+            d += __shfl_xor_sync(full, d, 8);
+            d += __shfl_xor_sync(full, d, 4);
+            d += __shfl_xor_sync(full, d, 2);
+            d += __shfl_xor_sync(full, d, 1);
+            sc[u][gi] = valid[u] ? d : -INFINITY;
+          }
+        }
+#pragma unroll
+        for (int gi = 0; gi < G; ++gi) {
+          float mt = sc[0][gi];
+#pragma unroll
+          for (int u = 1; u < kRowsPerHalf; ++u) mt = fmaxf(mt, sc[u][gi]);
+          const float mn = fmaxf(m[gi], mt);
+          if (mn == -INFINITY) continue;
+          const float alpha = ex2(m[gi] - mn);
+          float pr[kRowsPerHalf];
+          float ps = 0.f;
+#pragma unroll
+          for (int u = 0; u < kRowsPerHalf; ++u) {
+            pr[u] = ex2(sc[u][gi] - mn);
+            ps += pr[u];
+          }
+          l[gi] = l[gi] * alpha + ps;
+          m[gi] = mn;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[gi][e] *= alpha;
+#pragma unroll
+          for (int u = 0; u < kRowsPerHalf; ++u) {
+            float vf[8];
+            unpack8(vr[u], vf, kBf16);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[gi][e] = fmaf(pr[u], vf[e], acc[gi][e]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(s));
+    }
+  }
+  __syncthreads();  // the ring is idle from here on: reuse it for the merge
+
+  float* sm_m = reinterpret_cast<float*>(smem);            // [8][G]
+  float* sm_l = sm_m + 8 * G;                              // [8][G]
+  float* sm_acc = sm_l + 8 * G;                            // [8][G][kD]
+  if (warp < kBulkConsumerWarps) {
+    const int half = lane >> 4;
+    const int c = lane & 15;
+    const int grp = warp * 2 + half;
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) {
+      if (c == 0) {
+        sm_m[grp * G + gi] = m[gi];
+        sm_l[grp * G + gi] = l[gi];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sm_acc[(grp * G + gi) * kD + c * 8 + e] = acc[gi][e];
+    }
+  }
+  __syncthreads();
+  if (tid < kD) {
+    const int d = tid;
+    for (int gi = 0; gi < g && gi < G; ++gi) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) M = fmaxf(M, sm_m[r * G + gi]);
+      float L = 0.f, A = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const float w = ex2(sm_m[r * G + gi] - M);
+          L += w * sm_l[r * G + gi];
+          A += w * sm_acc[(r * G + gi) * kD + d];
+        }
+      }
+      const long long slot = (static_cast<long long>(b) * p.Hq + (hk * g + gi)) * p.splits + split;
+      p.part_acc[slot * kD + d] = A;
+      if (d == 0) {
+        p.part_ml[slot * 2] = M;
+        p.part_ml[slot * 2 + 1] = L;
+      }
+    }
+  }
+}
+
 // One CTA per (b, query head): merge the splits in index order.
 template <typename T>
 __global__ void __launch_bounds__(kD) decode_combine_kernel(const Params p) {
@@ -243,18 +490,42 @@ __global__ void __launch_bounds__(kD) decode_combine_kernel(const Params p) {
   op[d] = DT<T>::from_f(out);
 }
 
-template <typename T>
-static void launch_decode(const Params& p, int g, cudaStream_t s) {
+template <typename T, int G>
+static void launch_split(const Params& p, bool bulk, cudaStream_t s) {
   dim3 grid(p.splits, p.Hkv, p.B);
-  if (g <= 1)
-    decode_split_kernel<T, 1><<<grid, kThreads, 0, s>>>(p);
-  else if (g <= 2)
-    decode_split_kernel<T, 2><<<grid, kThreads, 0, s>>>(p);
-  else if (g <= 4)
-    decode_split_kernel<T, 4><<<grid, kThreads, 0, s>>>(p);
+  if (bulk)
+    decode_bulk_kernel<T, G><<<grid, kBulkThreads, kBulkSmem, s>>>(p);
   else
-    decode_split_kernel<T, 8><<<grid, kThreads, 0, s>>>(p);
+    decode_split_kernel<T, G><<<grid, kThreads, 0, s>>>(p);
+}
+
+// Bulk streaming needs rows contiguous per head and whole 64-row chunks per
+// block; other layouts use the register-streaming kernel.
+static bool bulk_layout(const Params& p) {
+  return p.k_st == kD && p.v_st == kD && p.block % kChunkRows == 0;
+}
+
+template <typename T>
+static cudaError_t launch_decode(const Params& p, int g, cudaStream_t s) {
+  const bool bulk = bulk_layout(p);
+  if (bulk) {
+    cudaError_t e = cudaSuccess;
+    if (g <= 1) e = cudaFuncSetAttribute(decode_bulk_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem);
+    else if (g <= 2) e = cudaFuncSetAttribute(decode_bulk_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem);
+    else if (g <= 4) e = cudaFuncSetAttribute(decode_bulk_kernel<T, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem);
+    else e = cudaFuncSetAttribute(decode_bulk_kernel<T, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem);
+    if (e != cudaSuccess) return e;
+  }
+  if (g <= 1)
+    launch_split<T, 1>(p, bulk, s);
+  else if (g <= 2)
+    launch_split<T, 2>(p, bulk, s);
+  else if (g <= 4)
+    launch_split<T, 4>(p, bulk, s);
+  else
+    launch_split<T, 8>(p, bulk, s);
   decode_combine_kernel<T><<<p.B * p.Hq, kD, 0, s>>>(p);
+  return cudaGetLastError();
 }
 
 }  // namespace decode
@@ -341,11 +612,11 @@ int sabre_decode_bsa(const void* q, const void* k_cache, const void* v_cache, vo
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int g = heads_q / heads_kv;
+  cudaError_t e;
   if (dtype == SABRE_BF16)
-    launch_decode<__nv_bfloat16>(p, g, s);
+    e = launch_decode<__nv_bfloat16>(p, g, s);
   else
-    launch_decode<__half>(p, g, s);
-  cudaError_t e = cudaGetLastError();
+    e = launch_decode<__half>(p, g, s);
   if (e != cudaSuccess) return sabre_cuda_fail(e, "sabre_decode_bsa launch");
   return SABRE_OK;
 }
@@ -492,11 +763,11 @@ int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_c
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int g = heads_q / heads_kv;
+  cudaError_t e;
   if (dtype == SABRE_BF16)
-    launch_decode<__nv_bfloat16>(p, g, s);
+    e = launch_decode<__nv_bfloat16>(p, g, s);
   else
-    launch_decode<__half>(p, g, s);
-  cudaError_t e = cudaGetLastError();
+    e = launch_decode<__half>(p, g, s);
   if (e != cudaSuccess) return sabre_cuda_fail(e, "sabre_decode_bsa_noalloc launch");
   return SABRE_OK;
 }

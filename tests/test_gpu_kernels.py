@@ -232,7 +232,8 @@ def test_pooled_topk_bit_exact(K, B, Hq, Hkv, L, block, topk):
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,Tmax,block,shared", [(1, 4, 4, 3000, 64, True), (2, 7, 1, 2048, 128, False),
-                                                         (3, 8, 2, 1500, 64, False), (1, 2, 2, 64, 64, True)])
+                                                         (3, 8, 2, 1500, 64, False), (1, 2, 2, 64, 64, True),
+                                                         (1, 16, 2, 5000, 64, False), (2, 4, 4, 700, 192, True)])
 def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
     gen = torch.Generator().manual_seed(Tmax + Hq)
     D = 128
@@ -252,6 +253,29 @@ def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
     out = K.decode_bsa(q.cuda(), kc.cuda(), vc.cuda(), bi.cuda(), bc.cuda(), seq.cuda(), block)
     torch.cuda.synchronize()
     ref = AO.sparse_decode_fp32(q, kc, vc, bi, bc, seq, block)
+    _close(out, ref)
+
+
+@pytest.mark.parametrize("block,row_pad", [(32, 0), (64, 128)])
+def test_decode_strided_cache_vs_oracle(K, block, row_pad):
+    """Caches whose rows are not contiguous per head (row stride > head_dim) or
+    blocks that are not whole 64-row chunks take the register-streaming kernel."""
+    gen = torch.Generator().manual_seed(block + row_pad)
+    B, Hq, Hkv, Tmax, D = 2, 4, 2, 1200, 128
+    q = torch.randn(B, Hq, D, generator=gen).to(torch.bfloat16)
+    kbig = torch.randn(B, Hkv, Tmax, D + row_pad, generator=gen).to(torch.bfloat16)
+    vbig = torch.randn(B, Hkv, Tmax, D + row_pad, generator=gen).to(torch.bfloat16)
+    seq = torch.tensor([Tmax, 777], dtype=torch.int32)
+    nbk = (Tmax + block - 1) // block
+    m = torch.rand(B, Hkv, nbk, generator=gen) < 0.5
+    for b in range(B):
+        m[b, :, (int(seq[b]) - 1) // block] = True
+    idx, cnt = MO.block_indices_from_mask(m.numpy())
+    bi, bc = torch.from_numpy(idx), torch.from_numpy(cnt)
+    kc, vc = kbig.cuda()[..., :D], vbig.cuda()[..., :D]
+    out = K.decode_bsa(q.cuda(), kc, vc, bi.cuda(), bc.cuda(), seq.cuda(), block)
+    torch.cuda.synchronize()
+    ref = AO.sparse_decode_fp32(q, kbig[..., :D], vbig[..., :D], bi, bc, seq, block)
     _close(out, ref)
 
 
