@@ -45,10 +45,26 @@ ARCH = {
                  num_attention_heads=16, num_key_value_heads=16),
     "6.7b": dict(vocab_size=32256, hidden_size=4096, intermediate_size=11008, num_hidden_layers=32,
                  num_attention_heads=32, num_key_value_heads=32),
+    "33b": dict(vocab_size=32256, hidden_size=7168, intermediate_size=19200, num_hidden_layers=62,
+                num_attention_heads=56, num_key_value_heads=8),
 }
 MASK = dict(block_size=64, window_size=192, num_prefix_tokens=64, num_suffix_tokens=128, max_chunk_tokens=128,
             global_last_k_chunks=0)
 TOPK = 8
+# The 33B workload: block 128 (4-block window), structure lists only.
+MASK_C4 = dict(block_size=128, window_size=384, num_prefix_tokens=128, num_suffix_tokens=128, max_chunk_tokens=128,
+               global_last_k_chunks=0)
+
+
+def mask_text(mask, topk) -> str:
+    return (f"block {mask['block_size']}, window {mask['window_size']}, sink {mask['num_prefix_tokens']}, "
+            f"suffix {mask['num_suffix_tokens']}, {mask['max_chunk_tokens']}-token chunk groups"
+            + (f", pooled top-{topk} per layer/head" if topk else ", structure lists only"))
+
+
+def mask_cfg(name: str):
+    """(mask builder parameters, pooled top-k) of a workload."""
+    return (MASK_C4, 0) if name == "c4" else (MASK, TOPK)
 
 
 def parse_args():
@@ -57,7 +73,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c0"], default="c1")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c0"], default="c1")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-only", action="store_true",
@@ -78,22 +94,21 @@ def workload(name: str, rank: int, world: int):
         return "1.3b", [(12288, 1000 + rank)], "weak"
     if name == "c3":
         return "6.7b", [(16384, 3000 + rank)], "weak"
+    if name == "c4":
+        # head-parallel: every rank works on the same prompt with its share of the heads
+        return "33b", [(16384, 4000)], "tp"
     if name == "c2":
         import numpy as np
+        from sabrecoder_b200.prompt_parallel import prompts_for_rank
         lens = np.random.default_rng(2).integers(12288, 16385, size=8).tolist()
-        order = sorted(range(8), key=lambda i: -lens[i])  # LPT over ranks
-        loads = [0] * world
-        mine = []
-        for i in order:
-            r = min(range(world), key=lambda j: loads[j])
-            loads[r] += lens[i]
-            if r == rank:
-                mine.append((int(lens[i]), 2000 + i))
-        return "1.3b", mine, "strong"
+        return "1.3b", [(int(lens[i]), 2000 + i) for i in prompts_for_rank(lens, rank, world)], "strong"
     return None, [(4096, 0)], "weak"
 
 
-def build_model(arch: str, device):
+def build_model(arch: str, device, rank: int = 0, world: int = 1):
+    """Random-init bf16 LLaMA of the named architecture. The 33B model is built
+    on the meta device, split head-parallel for (rank, world) and only this
+    rank's shard is given storage, so the full weights are never held."""
     import torch
     from transformers import LlamaConfig, LlamaForCausalLM
     cfg = LlamaConfig(**ARCH[arch], head_dim=128, max_position_embeddings=16384, rope_theta=100000.0,
@@ -103,8 +118,15 @@ def build_model(arch: str, device):
     prev = torch.get_default_dtype()
     torch.set_default_dtype(torch.bfloat16)
     try:
-        with torch.device(device):
-            model = LlamaForCausalLM(cfg)
+        if arch == "33b":
+            from sabrecoder_b200 import tensor_parallel as TP
+            with torch.device("meta"):
+                model = LlamaForCausalLM(cfg)
+            TP.shard_llama_(model, rank, world)
+            TP.materialize_random_(model, device, seed=0)
+        else:
+            with torch.device(device):
+                model = LlamaForCausalLM(cfg)
     finally:
         torch.set_default_dtype(prev)
     return model.eval(), cfg
@@ -202,10 +224,12 @@ def measured_peaks():
 # CPU side (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------
 
-def cpu_layer_sample(arch: str, L: int, seed: int, repeats: int = 1):
+def cpu_layer_sample(arch: str, L: int, seed: int, repeats: int = 1, mask=None, topk=None):
     """One decoder layer of the workload on the host cores with the reference's
     dense-masked attention arithmetic; returns (list of seconds per layer call,
-    layers, threads). Structure lists and pooled top-8 come from the oracle."""
+    layers, threads). Structure lists and pooled top-k come from the oracle."""
+    mask = MASK if mask is None else mask
+    topk = TOPK if topk is None else topk
     import numpy as np
     import torch
     from oracle import attention_oracle as AO
@@ -222,8 +246,8 @@ def cpu_layer_sample(arch: str, L: int, seed: int, repeats: int = 1):
     rot = LlamaRotaryEmbedding(cfg)
     _, spans = prompt_inputs(L, seed)
     base = MO.build_block_mask_tokens(spans.token_to_chunk(), len(spans.spans), spans.import_chunks, spans.deps,
-                                      spans.signature_token_mask(), seq_len=L, **MASK).astype(bool)
-    B = MASK["block_size"]
+                                      spans.signature_token_mask(), seq_len=L, **mask).astype(bool)
+    B = mask["block_size"]
     attn = layer.self_attn
 
     class DenseMasked(torch.nn.Module):
@@ -235,13 +259,18 @@ def cpu_layer_sample(arch: str, L: int, seed: int, repeats: int = 1):
             k = attn.k_proj(hidden_states).view(shp).transpose(1, 2)
             v = attn.v_proj(hidden_states).view(shp).transpose(1, 2)
             q, k = apply_rotary_pos_emb(q, k, *position_embeddings)
-            qm = MO.pooled_block_means(q.detach().numpy(), l, B)
-            km = MO.pooled_block_means(k.detach().numpy(), l, B)
-            ext = MO.topk_extend_mask(base, MO.pooled_scores(qm, km), TOPK)
+            grp = q.shape[1] // k.shape[1]
+            if topk > 0:
+                qm = MO.pooled_block_means(q.detach().numpy(), l, B)
+                km = MO.pooled_block_means(k.detach().numpy(), l, B)
+                ext = MO.topk_extend_mask(base, MO.pooled_scores(qm, km.repeat(grp, axis=1)), topk)
+            else:
+                ext = np.broadcast_to(base, (1, q.shape[1]) + base.shape)
             outs = []
             for h in range(q.shape[1]):  # one head at a time bounds host memory
-                outs.append(AO.dense_masked_sdpa(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1],
-                                                 torch.from_numpy(ext[0, h]), B))
+                hk = h // grp
+                outs.append(AO.dense_masked_sdpa(q[:, h:h + 1], k[:, hk:hk + 1], v[:, hk:hk + 1],
+                                                 torch.from_numpy(np.ascontiguousarray(ext[0, h])), B))
             o = torch.cat(outs, 1).transpose(1, 2).reshape(b, l, -1)
             return attn.o_proj(o), None
 
@@ -265,16 +294,18 @@ def run_reference_arm(args, rank, world):
     arch = arch or "1.3b"
     L, seed = prompts[0]
     # warm-up calls are folded into the same sample run and discarded
-    dts, layers, threads = cpu_layer_sample(arch, L, seed, repeats=min(args.warmup, 1) + args.steps)
+    mask, topk = mask_cfg(args.workload)
+    dts, layers, threads = cpu_layer_sample(arch, L, seed, repeats=min(args.warmup, 1) + args.steps, mask=mask,
+                                            topk=topk)
     times = [d * layers for d in dts[min(args.warmup, 1):]]
     per_prompt = statistics.mean(times)
     value = L / per_prompt
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_prompt * 1e3, "higher_is_better": True,
-        "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {arch} LLaMA prefill, {L} tokens, block 64, "
-                               "structure spans + pooled top-8", "seq_len": L, "global_batch": 1},
+        "scaling": "strong" if scaling == "tp" else scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {arch} LLaMA prefill, {L} tokens, {mask_text(mask, topk)}",
+                   "seq_len": L, "global_batch": 1},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"1 of {layers} decoder layers (fp32, dense-masked SDPA per head) on {L} "
                                    f"tokens, scaled x{layers}; embeddings/lm_head excluded"},
@@ -301,9 +332,11 @@ def run_ours(args, rank, world, dist):
         return run_decode_op(args, rank, world, dist)
     if arch is None or args.attn_only:
         return run_op_bench(args, rank, world, dist)
-    model, cfg = build_model(arch, dev)
-    SL.patch_model_with_sabrecoder_attention(model, None, topk_blocks=TOPK, verbose=False, **MASK)
-    mb = StructureAwareMaskBuilder(None, **MASK)
+    mask, topk = mask_cfg(args.workload)
+    tp = scaling == "tp"
+    model, cfg = build_model(arch, dev, rank, world) if tp else build_model(arch, dev)
+    SL.patch_model_with_sabrecoder_attention(model, None, topk_blocks=topk, verbose=False, **mask)
+    mb = StructureAwareMaskBuilder(None, **mask)
     SL.set_current_code("<synthetic prompt>")
 
     prepared = []
@@ -315,7 +348,8 @@ def run_ours(args, rank, world, dist):
     # One preallocated KV cache, refilled by every prefill (the fused RoPE
     # kernel writes K/V rows straight into it).
     from sabrecoder_b200.kv_cache import SabreKVCache
-    cache = SabreKVCache(cfg, batch_size=1, max_cache_len=max(p[0] for p in prepared) + 64, device=dev)
+    cache = SabreKVCache(cfg, batch_size=1, max_cache_len=max(p[0] for p in prepared) + 64, device=dev,
+                         num_kv_heads=cfg.num_key_value_heads // (world if tp else 1))
 
     def step():
         for L, ids_d, bi, bc, bm, _, _ in prepared:
@@ -370,6 +404,8 @@ def run_ours(args, rank, world, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_max = float(t.item())
     value = tokens_per_step * world * args.steps / (ms_max / 1e3) if scaling == "weak" else None
+    if tp:  # every rank prefills the same prompt with its share of the heads
+        value = tokens_per_step * args.steps / (ms_max / 1e3)
     if scaling == "strong":
         tot = torch.tensor([tokens_per_step], device=dev, dtype=torch.float64)
         if dist is not None:
@@ -390,7 +426,7 @@ def run_ours(args, rank, world, dist):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         L0, seed0 = prompts[0]
-        dts, layers, threads = cpu_layer_sample(arch, L0, seed0)
+        dts, layers, threads = cpu_layer_sample(arch, L0, seed0, mask=mask, topk=topk)
         v = L0 / (dts[0] * layers)
         cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
                "sample": f"1 of {layers} decoder layers (fp32, dense-masked SDPA per head) on {L0} tokens, "
@@ -400,12 +436,13 @@ def run_ours(args, rank, world, dist):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": "strong" if scaling == "tp" else scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"{args.workload}: {arch} LLaMA (random-init bf16) sparse prefill, "
-                                   f"{'+'.join(str(p[0]) for p in prepared)} tokens per GPU, block 64, window 192, "
-                                   f"sink 64, suffix 128, 128-token chunk groups, pooled top-{TOPK} per layer/head",
+                                   f"{'+'.join(str(p[0]) for p in prepared)} tokens "
+                                   f"{'per job' if tp else 'per GPU'}, {mask_text(mask, topk)}",
                        "seq_len": prepared[0][0], "global_batch": len(prompts) * (world if scaling == "weak" else 1),
-                       "parallelism": f"prompt-parallel x{world}, no collectives",
+                       "parallelism": (f"head-parallel TP x{world}: NCCL all-reduce after o_proj and down_proj"
+                                       if tp and world > 1 else f"prompt-parallel x{world}, no collectives"),
                        "l2": "inputs larger than L2 (2.6 GB of weights read per step)",
                        "density_structure": round(statistics.mean(dens), 4),
                        "density_with_topk": round(act / tot_blocks, 4) if tot_blocks else None},
@@ -480,6 +517,8 @@ def e2e_through_api(model, mb, prepared, args, dev, dist, cache):
     _, _, scaling = workload(args.workload, 0, world)
     if scaling == "weak":
         val = toks * world * args.steps / (ms / 1e3)
+    elif scaling == "tp":  # all ranks prefill the same prompt
+        val = toks * args.steps / (ms / 1e3)
     else:
         tt = torch.tensor([toks], device=dev, dtype=torch.float64)
         if dist is not None:
@@ -659,7 +698,8 @@ def main():
 
         import torch.distributed as tdist
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                 device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
         dist = tdist
     try:
         run_ours(args, rank, world, dist)
