@@ -8,17 +8,27 @@
 //
 // Design (one CTA = 128 query rows of one head; 224 threads; 2 CTAs per SM):
 //   warps 0-3  softmax + epilogue; thread t owns query row t = TMEM lane t
-//   warp 4     TMA producer for K (3-stage ring, a stage is released as soon
-//              as the S = Q K^T that read it completes)
+//   warp 4     TMA producer for Q and K (3-stage ring, a stage is released as
+//              soon as the S = Q K^T that read it completes)
 //   warp 5     TMEM allocator and single-thread tcgen05.mma issuer
 //   warp 6     TMA producer for V (2-stage ring, released when P.V completes)
+// Each tcgen05.commit costs the tensor pipe about as much as a small MMA, so
+// a key tile takes two: S_FULL[stage] after its S = Q K^T (read by the
+// softmax, and by the K producer as "stage free"), and P_EMPTY[buffer] after
+// its P.V (read by the softmax, and by the V producer: V stage i%2 and P
+// buffer i%2 are released by the same P.V). Each barrier's next completion
+// needs its waiter's own next step, so no waiter can miss a phase.
 // TMEM (256 columns): O [0,128), S [128,192), P0 [192,224), P1 [224,256).
 //   S = Q K^T      M=128 N=64  K=128, A and B from shared memory
 //   O += P V       M=128 N=128 K=64,  A (P, bf16 pairs) from TMEM, B (V)
 //                  from shared memory (MN-major)
 // Shared memory (bytes): Q 32768 | K 3x16384 | V 2x16384 | key-tile bitmaps
-// 256 | barriers (~112.5 KB). The Q buffer doubles as the staging tile of
-// the epilogue's TMA store of O.
+// 256 | barriers (~112.5 KB).
+// A CTA's fixed costs are kept off its critical path: the Q tile is
+// requested right after the barriers are set up, while the block lists are
+// still being read, and each softmax thread writes its finished output row
+// straight to global memory with 16-byte stores (no staging, no wait for a
+// bulk store to drain before the CTA can exit).
 //
 // The key-tile list of a CTA is the union of the lists of the (one or two)
 // query blocks its rows belong to, kept as two 1024-bit bitmaps (one per
@@ -55,11 +65,9 @@ constexpr int kBarOff = kBitsOff + 2 * kWords * 4;
 enum Bar {
   Q_FULL = 0,
   K_FULL = 1,                     // [3]
-  K_EMPTY = K_FULL + kKStages,    // [3]
-  V_FULL = K_EMPTY + kKStages,    // [2]
-  V_EMPTY = V_FULL + kVStages,    // [2]
-  S_FULL = V_EMPTY + kVStages,
-  S_EMPTY = S_FULL + 1,
+  V_FULL = K_FULL + kKStages,     // [2]
+  S_FULL = V_FULL + kVStages,     // [3] one per K stage; also "K stage free"
+  S_EMPTY = S_FULL + kKStages,
   P_FULL = S_EMPTY + 1,           // [2]
   P_EMPTY = P_FULL + 2,           // [2]
   MMA_DONE = P_EMPTY + 2,
@@ -72,6 +80,8 @@ constexpr uint32_t kTmemS = 128;
 constexpr uint32_t kTmemP = 192;  // + 32 * buffer
 
 struct Params {
+  void* o;                      // output rows, written with 16-byte stores
+  long long o_sb, o_sh, o_sl;   // element strides (d stride 1)
   const int32_t* idx;
   const int32_t* cnt;
   long long idx_sb, idx_sh, idx_sm, idx_sk;
@@ -103,8 +113,7 @@ struct UnionIter {
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_bsa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                       const Params p) {
+                       const __grid_constant__ CUtensorMap tmV, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -133,13 +142,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(bar(Q_FULL), 1);
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(bar(K_FULL + s), 1);
-      mbar_init(bar(K_EMPTY + s), 1);
+      mbar_init(bar(S_FULL + s), 1);
     }
-    for (int s = 0; s < kVStages; ++s) {
-      mbar_init(bar(V_FULL + s), 1);
-      mbar_init(bar(V_EMPTY + s), 1);
-    }
-    mbar_init(bar(S_FULL), 1);
+    for (int s = 0; s < kVStages; ++s) mbar_init(bar(V_FULL + s), 1);
     mbar_init(bar(S_EMPTY), 4);  // one arrival per softmax warp
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(P_FULL + s), 4);
@@ -147,10 +152,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     mbar_init(bar(MMA_DONE), 1);
     fence_mbar_init();
-    tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
-    tma_prefetch_desc(&tmO);
+    if ((sbase & 1023u) == 0u) {
+      mbar_arrive_expect_tx(bar(Q_FULL), kQBytes);
+      tma_load_4d(sbase + kQOff, &tmQ, bar(Q_FULL), 0, r0, h, b);
+      tma_load_4d(sbase + kQOff + kQBytes / 2, &tmQ, bar(Q_FULL), 64, r0, h, b);
+    }
   }
   if (warp == 5) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -197,15 +205,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool is_k = (warp == 4);
       const int stages = is_k ? kKStages : kVStages;
       const int full0 = is_k ? K_FULL : V_FULL;
-      const int empty0 = is_k ? K_EMPTY : V_EMPTY;
+      // K stage s is free when S_FULL[s] completes, V stage s when P_EMPTY[s] does.
+      const int empty0 = is_k ? S_FULL : P_EMPTY;
       const uint32_t ring = sbase + (is_k ? kKOff : kVOff);
       const CUtensorMap* map = is_k ? &tmK : &tmV;
       int issued[kKStages] = {0, 0, 0};
-      if (is_k) {
-        mbar_arrive_expect_tx(bar(Q_FULL), kQBytes);
-        tma_load_4d(sbase + kQOff, &tmQ, bar(Q_FULL), 0, r0, h, b);
-        tma_load_4d(sbase + kQOff + kQBytes / 2, &tmQ, bar(Q_FULL), 64, r0, h, b);
-      }
       UnionIter it(bits, bits + kWords, nw);
       for (int j = 0;; ++j) {
         const int kt = it.next();
@@ -247,7 +251,6 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int kk = 1; kk < 4; ++kk) mma_f16_ts(tmem, pa + 8 * kk, vd + kk * (2048 >> 4), kIdescPV, 1u);
         mma_commit(bar(P_EMPTY + pb));
-        mma_commit(bar(V_EMPTY + pb));
         return true;
       };
       for (int j = 0; ok && j < n; ++j) {
@@ -262,8 +265,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint64_t ko = ((kk >> 2) * (kKVStageBytes / 2) + (kk & 3) * 32) >> 4;
           mma_f16_ss(s_tmem, qd + qo, kd + ko, kIdescQK, kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar(S_FULL));
-        mma_commit(bar(K_EMPTY + ks));
+        mma_commit(bar(S_FULL + ks));
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok && n >= 1) issue_pv(n - 1);
@@ -284,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     UnionIter it(bits, bits + kWords, nw);
     for (int j = 0; ok && j < n; ++j) {
       const int kt = it.next();
-      ok = mbar_wait_warp(bar(S_FULL), j & 1, abort_flag);
+      ok = mbar_wait_warp(bar(S_FULL + j % kKStages), (j / kKStages) & 1, abort_flag);
       if (!ok) break;
       tc_fence_after();
       uint32_t sr0[32], sr1[32];
@@ -362,21 +364,22 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(P_FULL + pb));
     }
-    // Epilogue: O / l, staged as a swizzled [128][64] x 2 tile in the Q buffer
-    // (free once the last P.V completed) and written by a TMA store.
+    // Epilogue: O / l, each thread stores its own row (256 bytes).
     if (ok && n >= 1) {
       ok = mbar_wait(bar(P_EMPTY + ((n - 1) & 1)), ((n - 1) >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
     } else if (ok) {
-      // No key tile: nothing consumed Q, so its load may still be landing in
-      // the buffer the output is staged in.
+      // No key tile: the Q load issued at the start must land before the CTA exits.
       ok = mbar_wait(bar(Q_FULL), 0, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
     }
     ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
+    // After a timeout anywhere in the CTA the tile is incomplete: store nothing.
+    if (ok && *abort_flag == 0) {
       const float inv = (l_run > 0.f) ? 1.0f / l_run : 0.0f;
+      T* orow = static_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh + static_cast<long long>(r_abs) * p.o_sl;
+      const bool row_ok = r_abs < p.L;
 #pragma unroll 1
       for (int ch = 0; ch < 4; ++ch) {
         uint32_t ov[32];
@@ -391,24 +394,13 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int c = 0; c < 32; c += 2)
           pkd[c >> 1] = DT<T>::pack(__uint_as_float(ov[c]) * inv, __uint_as_float(ov[c + 1]) * inv);
-        // columns [32ch, 32ch+32) = d-half ch/2, 16-byte chunks 4*(ch&1) .. +3
-        uint8_t* rowp = smem + kQOff + (ch >> 1) * (kQBytes / 2) + row * 128;
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int chunk = 4 * (ch & 1) + q4;
-          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) =
-              make_uint4(pkd[4 * q4], pkd[4 * q4 + 1], pkd[4 * q4 + 2], pkd[4 * q4 + 3]);
+          for (int q4 = 0; q4 < 4; ++q4)
+            dst[q4] = make_uint4(pkd[4 * q4], pkd[4 * q4 + 1], pkd[4 * q4 + 2], pkd[4 * q4 + 3]);
         }
       }
-      fence_proxy_async_smem();
-    }
-    named_bar_sync(1, 128);
-    // After a timeout anywhere in the CTA the tile is incomplete: skip the store.
-    if (tid == 0 && start_ok && *abort_flag == 0) {
-      tma_store_4d(&tmO, sbase + kQOff, 0, r0, h, b);
-      tma_store_4d(&tmO, sbase + kQOff + kQBytes / 2, 64, r0, h, b);
-      tma_store_commit();
-      tma_store_wait_read();
     }
   }
 

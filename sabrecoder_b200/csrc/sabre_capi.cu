@@ -157,11 +157,8 @@ int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, cons
     if ((o_strides[i] * 2) % 16 != 0)
       return fail(SABRE_ERR_ALIGNMENT, "sabre_prefill_bsa: o stride %d not a 16-byte multiple", i);
 
-  CUtensorMap mq, mk, mv, mo;
+  CUtensorMap mq, mk, mv;
   int st;
-  if ((st = make_map_bhld(&mo, o, dtype, batch, heads_q, seq_len, head_dim, o_strides[0], o_strides[1],
-                          o_strides[2], kTileM, "o")) != SABRE_OK)
-    return st;
   if ((st = make_map_bhld(&mq, q, dtype, batch, heads_q, seq_len, head_dim, q_strides[0], q_strides[1],
                           q_strides[2], kTileM, "q")) != SABRE_OK)
     return st;
@@ -173,6 +170,10 @@ int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, cons
     return st;
 
   Params p;
+  p.o = o;
+  p.o_sb = o_strides[0];
+  p.o_sh = o_strides[1];
+  p.o_sl = o_strides[2];
   p.idx = block_indices;
   p.cnt = block_counts;
   p.idx_sb = idx_strides[0];
@@ -199,10 +200,10 @@ int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, cons
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SABRE_BF16) {
     if ((st = ensure_smem_attr(prefill_bsa_kernel<__nv_bfloat16>, kSmemBytes)) != SABRE_OK) return st;
-    prefill_bsa_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, mo, p);
+    prefill_bsa_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
   } else {
     if ((st = ensure_smem_attr(prefill_bsa_kernel<__half>, kSmemBytes)) != SABRE_OK) return st;
-    prefill_bsa_kernel<__half><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, mo, p);
+    prefill_bsa_kernel<__half><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
   }
   SABRE_CUDA_TRY(cudaGetLastError());
   return SABRE_OK;
