@@ -34,7 +34,7 @@ typedef enum {
   SABRE_ERR_WORKSPACE = -5     /* workspace missing or too small */
 } sabre_status_t;
 
-enum { SABRE_BF16 = 0, SABRE_F16 = 1 };
+enum { SABRE_BF16 = 0, SABRE_F16 = 1, SABRE_F32 = 2 /* sabre_chunk_vectors embeddings only */ };
 
 /* Device status flags (sabre_device_status). */
 enum { SABRE_DEV_TIMEOUT = 1u, SABRE_DEV_BAD_SMEM_ALIGN = 2u };
@@ -220,6 +220,34 @@ int sabre_topk_extend(const float* q_pooled, const float* k_pooled, const uint32
                       int heads_q, int heads_kv, int num_blocks, int head_dim, int topk, int32_t* indices,
                       int cap, int32_t* counts, int32_t* max_active_out, uint32_t* out_bits, void* workspace,
                       size_t workspace_bytes, void* stream);
+
+/* ----------------------------------------------------------------------
+ * (3d) Chunk-similarity dependency edges.
+ * Replaces StructureAwareMaskBuilder._get_or_build_similarity_vectors and
+ * _similarity_edges (methods/sabrecoder/sabrecoder_attention_triton.py:490-682);
+ * the caller keeps the text side (cleaning, tokenising, choosing k).
+ *
+ * sabre_chunk_vectors: embedding [vocab, dim] (SABRE_BF16, SABRE_F16 or
+ *   SABRE_F32, contiguous); chunk c owns tok_ids[tok_ptr[c] .. tok_ptr[c+1]).
+ *   out_f16 [nchunks, dim] = fp16(v / max(||v||, 1e-12)) with v the fp32 mean
+ *   of the chunk's embedding rows (tokens added first to last; an empty chunk
+ *   gives zeros). ||v||: thread t of 256 adds the squares of d = t, t+256, ...
+ *   in order, then a halving tree over the 256 partials. dim <= 8192; token
+ *   ids must lie in [0, vocab) (others are skipped).
+ * sabre_similarity_topk: for source s (vector row src_rows[s], chunk
+ *   src_chunk[s]) score every target t (row tgt_rows[t], chunk tgt_chunk[t]):
+ *   fp32 dot product, lane l of 32 adding the rounded products of
+ *   d = l, l+32, ... in order, then an xor tree (16, 8, 4, 2, 1); -inf when
+ *   tgt_chunk[t] == src_chunk[s]. Keeps the min(k, ntgt) best (value
+ *   descending, ties to the lower t) and writes their target chunk ids to
+ *   out_tgt_chunk [nsrc, k], -1 for the chunk itself and for unused slots.
+ *   k <= 64; ntgt <= 40960.
+ * ---------------------------------------------------------------------- */
+int sabre_chunk_vectors(const void* embedding, int emb_dtype, int vocab, int dim, const int32_t* tok_ptr,
+                        const int32_t* tok_ids, int nchunks, void* out_f16, void* stream);
+int sabre_similarity_topk(const void* vecs_f16, int dim, const int32_t* src_rows, const int32_t* src_chunk,
+                          int nsrc, const int32_t* tgt_rows, const int32_t* tgt_chunk, int ntgt, int k,
+                          int32_t* out_tgt_chunk, void* stream);
 
 #ifdef __cplusplus
 }

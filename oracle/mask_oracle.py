@@ -385,3 +385,145 @@ def topk_extend_mask(mask: np.ndarray, scores: np.ndarray, topk: int) -> np.ndar
             order = np.lexsort((cand, -sc))
             fm[r, qb, cand[order[:topk]]] = True
     return m
+
+
+# ---------------------------------------------------------------------------
+# Chunk-similarity edges (sabrecoder_attention_triton.py:458-682)
+# ---------------------------------------------------------------------------
+
+def clean_for_similarity(text: str) -> str:
+    """Drop a leading "# " or "// " from every line (reference :458-472)."""
+    out = []
+    for ln in text.split("\n"):
+        if ln.startswith("# "):
+            out.append(ln[2:])
+        elif ln.startswith("// "):
+            out.append(ln[3:])
+        else:
+            out.append(ln)
+    return "\n".join(out)
+
+
+def tokenize_for_similarity(tokenizer, texts, max_tokens: int):
+    """Token id lists as the reference obtains them (:526-554): one batched
+    call with truncation and padding (ids where the attention mask is set),
+    else ``encode`` per text cut to ``max_tokens``."""
+    try:
+        enc = tokenizer(texts, add_special_tokens=False, truncation=True, max_length=int(max_tokens),
+                        padding=True, return_tensors="pt")
+        ids, am = enc.get("input_ids", None), enc.get("attention_mask", None)
+        if ids is None or am is None:
+            raise RuntimeError("no input_ids/attention_mask")
+        ids = np.asarray(ids)
+        am = np.asarray(am)
+        return [[int(t) for t, m in zip(ids[r], am[r]) if m] for r in range(ids.shape[0])]
+    except Exception:  # noqa: BLE001 -- the reference falls back on any failure
+        out = []
+        for t in texts:
+            e = tokenizer.encode(t, add_special_tokens=False) if t and t.strip() else []
+            out.append([int(x) for x in e[: int(max_tokens)]])
+        return out
+
+
+def chunk_vectors_f16(embedding: np.ndarray, token_lists) -> np.ndarray:
+    """fp16 unit vectors of the chunks' mean token embeddings, every fp32
+    reduction in the order sabre_chunk_vectors uses: tokens added first to
+    last; squares of d = t, t+256, ... added in order per t, then a halving
+    tree over the 256 partials; v / max(sqrt(.), 1e-12)."""
+    emb = np.asarray(embedding, dtype=np.float32)
+    V, D = emb.shape
+    T = 256
+    P = (D + T - 1) // T
+    out = np.zeros((len(token_lists), D), dtype=np.float16)
+    for c, ids in enumerate(token_lists):
+        s = np.zeros(D, dtype=np.float32)
+        for i in ids:
+            if 0 <= int(i) < V:
+                s = (s + emb[int(i)]).astype(np.float32)
+        m = (s / np.float32(max(len(ids), 1))).astype(np.float32)
+        pad = np.zeros(P * T, dtype=np.float32)
+        pad[:D] = m
+        sq = (pad * pad).astype(np.float32).reshape(P, T)
+        part = np.zeros(T, dtype=np.float32)
+        for i in range(P):
+            part = (part + sq[i]).astype(np.float32)
+        h = T // 2
+        while h > 0:
+            part[:h] = (part[:h] + part[h:2 * h]).astype(np.float32)
+            h //= 2
+        denom = np.maximum(np.sqrt(part[0]).astype(np.float32), np.float32(1e-12))
+        out[c] = (m / denom).astype(np.float32).astype(np.float16)
+    return out
+
+
+def similarity_scores(a16: np.ndarray, b16: np.ndarray) -> np.ndarray:
+    """fp32 dot products of one fp16 vector with rows of ``b16`` in the order
+    sabre_similarity_topk uses: lane l of 32 adds the products of
+    d = l, l+32, ... in order, then an xor tree with strides 16, 8, 4, 2, 1."""
+    W = 32
+    D = a16.shape[0]
+    P = (D + W - 1) // W
+    pa = np.zeros(P * W, dtype=np.float32)
+    pa[:D] = a16.astype(np.float32)
+    pb = np.zeros((b16.shape[0], P * W), dtype=np.float32)
+    pb[:, :D] = b16.astype(np.float32)
+    prod = (pb * pa).astype(np.float32).reshape(b16.shape[0], P, W)
+    lane = np.zeros((b16.shape[0], W), dtype=np.float32)
+    for i in range(P):
+        lane = (lane + prod[:, i, :]).astype(np.float32)
+    idx = np.arange(W)
+    for o in (16, 8, 4, 2, 1):
+        lane = (lane + lane[:, idx ^ o]).astype(np.float32)
+    return lane[:, 0]
+
+
+def similarity_topk(vecs16: np.ndarray, src_rows, src_chunks, tgt_rows, tgt_chunks, k: int):
+    """Per source, the target chunk ids of the min(k, ntgt) best scores
+    (descending, ties to the lower target position), the chunk itself -1."""
+    tr = np.asarray(tgt_rows, dtype=np.int64)
+    tc = np.asarray(tgt_chunks, dtype=np.int64)
+    out = []
+    for r, c in zip(src_rows, src_chunks):
+        sc = similarity_scores(vecs16[int(r)], vecs16[tr])
+        sc = np.where(tc == int(c), np.float32(-np.inf), sc)
+        order = sorted(range(len(tc)), key=lambda j: (-float(sc[j]), j))[: min(int(k), len(tc))]
+        out.append([-1 if int(tc[j]) == int(c) else int(tc[j]) for j in order])
+    return out
+
+
+def similarity_edges(chunk_texts, tokenizer, embedding, *, top_percent: float, max_tokens: int,
+                     max_neighbors: int, src_indices=None, tgt_indices=None):
+    """Directed chunk-similarity edges {src: {tgt}} (reference :581-682)."""
+    frac = float(top_percent)
+    if frac > 1.0:
+        frac /= 100.0
+    frac = max(0.0, min(1.0, frac))
+    if int(max_neighbors) <= 0 or frac <= 0.0:
+        return {}
+    n = len(chunk_texts)
+    src = list(range(n)) if src_indices is None else list(src_indices)
+    tgt = list(range(n)) if tgt_indices is None else list(tgt_indices)
+    texts, idx_map = [], []
+    for i, t in enumerate(chunk_texts):
+        cl = clean_for_similarity(t or "")
+        if cl and cl.strip():
+            texts.append(cl)
+            idx_map.append(i)
+    if not idx_map:
+        return {}
+    vecs = chunk_vectors_f16(embedding, tokenize_for_similarity(tokenizer, texts, max_tokens))
+    row_of = {c: r for r, c in enumerate(idx_map)}
+    sr = [(c, row_of[c]) for c in src if c in row_of]
+    tg = [(c, row_of[c]) for c in tgt if c in row_of]
+    if not sr or not tg:
+        return {}
+    k = min(int(max_neighbors), int(np.floor(len(tg) * frac)))
+    if k <= 0:
+        return {}
+    picks = similarity_topk(vecs, [r for _, r in sr], [c for c, _ in sr], [r for _, r in tg], [c for c, _ in tg], k)
+    edges = {}
+    for (c, _), row in zip(sr, picks):
+        for t in row:
+            if t >= 0:
+                edges.setdefault(int(c), set()).add(int(t))
+    return edges

@@ -42,6 +42,8 @@ SIGNATURES = {
     "sabre_topk_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "sabre_topk_extend": (c_int, [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, c_int, P, P, P, P,
                                   c_size_t, P]),
+    "sabre_chunk_vectors": (c_int, [P, c_int, c_int, c_int, P, P, c_int, P, P]),
+    "sabre_similarity_topk": (c_int, [P, c_int, P, P, c_int, P, P, c_int, c_int, P, P]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

@@ -14,6 +14,7 @@
 #include "block_mask.cu"
 #include "rope_cache.cu"
 #include "topk.cu"
+#include "similarity.cu"
 
 #define SABRE_VERSION 100
 

@@ -310,3 +310,52 @@ def device_status(clear: bool = True, stream: Optional[int] = None) -> int:
                                            else None)
     check(lib().sabre_device_status(ctypes.byref(v), 1 if clear else 0, s), "sabre_device_status")
     return int(v.value)
+
+
+# ---------------------------------------------------------------------------
+# (3d) chunk-similarity edges
+# ---------------------------------------------------------------------------
+
+_EMB_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+
+def chunk_vectors(embedding: torch.Tensor, tok_ptr: torch.Tensor, tok_ids: torch.Tensor) -> torch.Tensor:
+    """fp16 ``[nchunks, dim]`` unit vectors: the fp32 mean of each chunk's
+    embedding rows, L2-normalised (sabre_chunk_vectors). ``tok_ptr`` int32
+    ``[nchunks + 1]`` and ``tok_ids`` int32 are CSR token lists on the
+    embedding's device."""
+    _need_cuda(embedding=embedding, tok_ptr=tok_ptr, tok_ids=tok_ids)
+    if embedding.dtype not in _EMB_CODE or embedding.dim() != 2:
+        raise SabreError("embedding must be a 2-D bf16, f16 or f32 tensor")
+    emb = embedding.contiguous()
+    _i32(tok_ptr, "tok_ptr")
+    _i32(tok_ids, "tok_ids")
+    n = tok_ptr.numel() - 1
+    out = torch.empty(max(n, 0), emb.shape[1], dtype=torch.float16, device=emb.device)
+    st = lib().sabre_chunk_vectors(emb.data_ptr(), _EMB_CODE[emb.dtype], emb.shape[0], emb.shape[1],
+                                   tok_ptr.data_ptr(), tok_ids.data_ptr() if tok_ids.numel() else None, n,
+                                   out.data_ptr(), _stream(emb))
+    check(st, "sabre_chunk_vectors")
+    LAUNCHES[0] += 1
+    return out
+
+
+def similarity_topk(vecs: torch.Tensor, src_rows: torch.Tensor, src_chunk: torch.Tensor, tgt_rows: torch.Tensor,
+                    tgt_chunk: torch.Tensor, k: int) -> torch.Tensor:
+    """int32 ``[nsrc, k]``: for each source the target chunk ids of its ``k``
+    best-scoring targets (sabre_similarity_topk); -1 for the chunk itself and
+    unused slots."""
+    _need_cuda(vecs=vecs, src_rows=src_rows, tgt_rows=tgt_rows)
+    if vecs.dtype != torch.float16 or not vecs.is_contiguous():
+        raise SabreError("vecs must be contiguous fp16")
+    for name, t in (("src_rows", src_rows), ("src_chunk", src_chunk), ("tgt_rows", tgt_rows),
+                    ("tgt_chunk", tgt_chunk)):
+        _i32(t, name)
+    ns, nt = src_rows.numel(), tgt_rows.numel()
+    out = torch.empty(ns, k, dtype=torch.int32, device=vecs.device)
+    st = lib().sabre_similarity_topk(vecs.data_ptr(), vecs.shape[1], src_rows.data_ptr(), src_chunk.data_ptr(), ns,
+                                     tgt_rows.data_ptr(), tgt_chunk.data_ptr(), nt, int(k), out.data_ptr(),
+                                     _stream(vecs))
+    check(st, "sabre_similarity_topk")
+    LAUNCHES[0] += 1
+    return out

@@ -40,6 +40,8 @@ _GLOBAL_CHUNK_CACHE: "OrderedDict" = OrderedDict()
 _GLOBAL_LINE_TO_TOKEN_CACHE: "OrderedDict" = OrderedDict()
 _GLOBAL_MASK_CACHE: "OrderedDict" = OrderedDict()
 _BLOCK_MASK_CACHE: "OrderedDict" = OrderedDict()
+_GLOBAL_SIM_VEC_CACHE: "OrderedDict" = OrderedDict()
+_GLOBAL_SIM_EDGES_CACHE: "OrderedDict" = OrderedDict()
 _GLOBAL_CACHE_MAX_SIZE = 50
 
 
@@ -334,6 +336,16 @@ class StructureAwareMaskBuilder:
     def build_block_indices_from_chunks(self, code: str, seq_len: int, device, *, chunks: List,
                                         chunk_deps: Dict[int, Set[int]], import_chunks: Set[int],
                                         language: Optional[str] = None, batch_size: int = 1):
+        """Index lists for given chunks and dependency edges; with
+        ``use_chunk_similarity`` the similarity edges are merged in first
+        (without changing the caller's dict), as the reference does (:1798-1805)."""
+        if self.use_chunk_similarity:
+            sim = self._similarity_edges(chunks, code)
+            if sim:
+                merged = {k: set(v) for k, v in (chunk_deps or {}).items()}
+                for src, tgts in sim.items():
+                    merged.setdefault(src, set()).update(tgts)
+                chunk_deps = merged
         dense = self._build_block_mask_from_chunks(code=code, seq_len=seq_len, chunks=chunks, chunk_deps=chunk_deps,
                                                    import_chunks=import_chunks, language=language, device=device)
         bi, bc = self._indices_from_bits(self.last_block_bits, dense.shape[0], batch_size)
@@ -359,8 +371,6 @@ class StructureAwareMaskBuilder:
             raise NotImplementedError("cross-file prompt chunking (sabrecoder_attention_triton.py:1622-1772) is "
                                       "not part of this library; segment the prompt and call "
                                       "build_block_indices_from_chunks")
-        if self.use_chunk_similarity:
-            raise NotImplementedError("chunk-similarity edges are not implemented; pass use_chunk_similarity=False")
         key = (hash(code), str(language).lower() if language else None)
         hit = _GLOBAL_CHUNK_CACHE.get(key)
         if hit is None:
@@ -378,6 +388,132 @@ class StructureAwareMaskBuilder:
         return self.build_block_indices_from_chunks(code, seq_len, device, chunks=hit["chunks"],
                                                     chunk_deps=hit["chunk_deps"], import_chunks=hit["import_chunks"],
                                                     language=language, batch_size=batch_size)
+
+    # ------------------------------------------------------------------
+    # Chunk-similarity edges (reference :458-682)
+    # ------------------------------------------------------------------
+    @staticmethod
+    def _clean_for_similarity(text: str) -> str:
+        """Drop a leading "# " or "// " from every line: cross-file context is
+        stored as commented code and the comment marks should not dominate
+        the embedding (reference :458-472)."""
+        out = []
+        for ln in text.split("\n"):
+            if ln.startswith("# "):
+                out.append(ln[2:])
+            elif ln.startswith("// "):
+                out.append(ln[3:])
+            else:
+                out.append(ln)
+        return "\n".join(out)
+
+    def _similarity_token_lists(self, texts: List[str]) -> List[List[int]]:
+        """One batched tokenizer call with truncation and padding (ids where the
+        attention mask is set); a tokenizer without that interface is called
+        per text through ``encode`` (reference :526-554)."""
+        cap = int(self.chunk_similarity_max_tokens_per_chunk)
+        try:
+            enc = self.tokenizer(texts, add_special_tokens=False, truncation=True, max_length=cap, padding=True,
+                                 return_tensors="pt")
+            ids, am = enc.get("input_ids", None), enc.get("attention_mask", None)
+            if ids is None or am is None:
+                raise RuntimeError("tokenizer returned no input_ids/attention_mask")
+            ids = torch.as_tensor(ids).cpu().numpy()
+            am = torch.as_tensor(am).cpu().numpy().astype(bool)
+            return [ids[r][am[r]].tolist() for r in range(ids.shape[0])]
+        except Exception:  # noqa: BLE001 -- same fallback as the reference
+            return [list(self.tokenizer.encode(t, add_special_tokens=False))[:cap] if t and t.strip() else []
+                    for t in texts]
+
+    def _device_embedding(self) -> torch.Tensor:
+        emb = self.embedding_weight
+        if emb is None:
+            raise RuntimeError("embedding_weight is required for chunk similarity but is None.")
+        if emb.is_cuda:
+            return emb.detach()
+        dev = self.device if self.device is not None and torch.device(self.device).type == "cuda" else "cuda"
+        key = ("emb", emb.data_ptr(), tuple(emb.shape), str(emb.dtype), str(dev))
+        hit = _GLOBAL_SIM_VEC_CACHE.get(key)
+        if hit is None:
+            hit = emb.detach().to(dev)
+            _cache_put(_GLOBAL_SIM_VEC_CACHE, key, hit)
+        return hit
+
+    def _get_or_build_similarity_vectors(self, chunks: List, code: str) -> Tuple[torch.Tensor, List[int]]:
+        """``(vectors fp16 [M, D] on the GPU, idx_map)``: one unit vector per
+        chunk whose cleaned text is not blank, ``idx_map[row]`` its chunk index
+        (reference :490-579). Vectors come from sabre_chunk_vectors."""
+        emb = self._device_embedding()
+        tok_key = getattr(self.tokenizer, "name_or_path", None) or type(self.tokenizer).__name__
+        key = (hash(code), tok_key, int(self.chunk_similarity_max_tokens_per_chunk), str(emb.device),
+               str(emb.dtype), int(emb.data_ptr()))
+        hit = _GLOBAL_SIM_VEC_CACHE.get(key)
+        if hit is not None:
+            return hit[0], list(hit[1])
+        texts, idx_map = [], []
+        for i, c in enumerate(chunks):
+            cleaned = self._clean_for_similarity(getattr(c, "text", "") or "")
+            if cleaned and cleaned.strip():
+                texts.append(cleaned)
+                idx_map.append(i)
+        if not texts:
+            mat = torch.empty(0, emb.shape[1], dtype=torch.float16, device=emb.device)
+        else:
+            lists = self._similarity_token_lists(texts)
+            vocab = emb.shape[0]
+            for ids in lists:
+                if any(t < 0 or t >= vocab for t in ids):
+                    raise IndexError(f"token id outside the embedding table of {vocab} rows")
+            ptr = np.zeros(len(lists) + 1, dtype=np.int32)
+            ptr[1:] = np.cumsum([len(x) for x in lists])
+            flat = np.asarray([t for x in lists for t in x], dtype=np.int32)
+            mat = K.chunk_vectors(emb, torch.from_numpy(ptr).to(emb.device),
+                                  torch.from_numpy(flat).to(emb.device))
+        _cache_put(_GLOBAL_SIM_VEC_CACHE, key, (mat, list(idx_map)))
+        return mat, list(idx_map)
+
+    def _similarity_edges(self, chunks: List, code: str, *, src_indices: Optional[List[int]] = None,
+                          tgt_indices: Optional[List[int]] = None,
+                          top_percent: Optional[float] = None) -> Dict[int, Set[int]]:
+        """Directed edges {source chunk: {target chunks}}: each source's
+        ``k = min(max_neighbors, floor(top_frac * num_targets))`` most similar
+        targets, itself excluded (reference :581-682). Exact score ties go to
+        the lower target position."""
+        if not self.use_chunk_similarity:
+            return {}
+        frac = float(self.chunk_similarity_top_percent) if top_percent is None else float(top_percent)
+        if frac > 1.0:  # a percentage
+            frac /= 100.0
+        frac = max(0.0, min(1.0, frac))
+        if self.chunk_similarity_max_neighbors <= 0 or frac <= 0.0:
+            return {}
+        src = list(range(len(chunks))) if src_indices is None else list(src_indices)
+        tgt = list(range(len(chunks))) if tgt_indices is None else list(tgt_indices)
+        key = (hash(code), frac, self.chunk_similarity_max_tokens_per_chunk, self.chunk_similarity_max_neighbors,
+               hash(tuple(src)), hash(tuple(tgt)))
+        hit = _GLOBAL_SIM_EDGES_CACHE.get(key)
+        if hit is not None:
+            return {k: set(v) for k, v in hit.items()}
+        mat, idx_map = self._get_or_build_similarity_vectors(chunks, code)
+        edges: Dict[int, Set[int]] = {}
+        row_of = {c: r for r, c in enumerate(idx_map)}
+        sr = [(c, row_of[c]) for c in src if c in row_of]
+        tg = [(c, row_of[c]) for c in tgt if c in row_of]
+        k = min(int(self.chunk_similarity_max_neighbors), int(math.floor(len(tg) * frac))) if tg else 0
+        if sr and tg and k > 0:
+            dev = mat.device
+
+            def i32(xs):
+                return torch.tensor(xs, dtype=torch.int32, device=dev)
+
+            picks = K.similarity_topk(mat, i32([r for _, r in sr]), i32([c for c, _ in sr]),
+                                      i32([r for _, r in tg]), i32([c for c, _ in tg]), k).cpu().numpy()
+            for (c, _), row in zip(sr, picks):
+                for t in row:
+                    if t >= 0:
+                        edges.setdefault(int(c), set()).add(int(t))
+        _cache_put(_GLOBAL_SIM_EDGES_CACHE, key, {k_: set(v) for k_, v in edges.items()})
+        return edges
 
     def _structure_backends(self):
         seg, ana = self.segmenter_factory, self.analyzer_factory
@@ -563,7 +699,8 @@ def print_cache_stats() -> None:
 
 
 def clear_all_caches() -> None:
-    for c in (_GLOBAL_CHUNK_CACHE, _GLOBAL_LINE_TO_TOKEN_CACHE, _GLOBAL_MASK_CACHE, _BLOCK_MASK_CACHE):
+    for c in (_GLOBAL_CHUNK_CACHE, _GLOBAL_LINE_TO_TOKEN_CACHE, _GLOBAL_MASK_CACHE, _BLOCK_MASK_CACHE,
+              _GLOBAL_SIM_VEC_CACHE, _GLOBAL_SIM_EDGES_CACHE):
         c.clear()
 
 

@@ -202,6 +202,67 @@ class WordTokenizer:
         return out
 
 
+class HashTokenizer:
+    """Tokenizer stand-in whose ids depend on the text: words (split on spaces
+    and newlines) map to a stable hash modulo ``vocab``. Offers the batched
+    call (padding, ``return_tensors="pt"``, attention mask) and ``encode``
+    that the chunk-similarity text side uses, plus offsets like
+    :class:`WordTokenizer` for the token-to-line mapping."""
+
+    name_or_path = "hash-tokenizer"
+
+    def __init__(self, vocab: int = 512):
+        self.vocab = int(vocab)
+
+    def _words(self, text):
+        spans = []
+        i, n = 0, len(text)
+        while i < n:
+            if text[i] in " \n":
+                i += 1
+                continue
+            j = i
+            while j < n and text[j] not in " \n":
+                j += 1
+            spans.append((i, j))
+            i = j
+        return spans
+
+    def _id(self, word: str) -> int:
+        h = 2166136261
+        for ch in word.encode("utf-8"):
+            h = ((h ^ ch) * 16777619) & 0xFFFFFFFF
+        return h % self.vocab
+
+    def encode(self, text, add_special_tokens=False, **kw):
+        return [self._id(text[a:b]) for a, b in self._words(text)]
+
+    def __call__(self, text, add_special_tokens=True, truncation=True, max_length=None, padding=False,
+                 return_tensors=None, return_offsets_mapping=False, **kw):
+        def one(t):
+            offs = self._words(t)
+            ids = [self._id(t[a:b]) for a, b in offs]
+            if truncation and max_length is not None:
+                ids, offs = ids[:max_length], offs[:max_length]
+            return ids, offs
+
+        if isinstance(text, (list, tuple)):
+            rows = [one(t)[0] for t in text]
+            width = max((len(r) for r in rows), default=0)
+            ids = [r + [0] * (width - len(r)) for r in rows]
+            mask = [[1] * len(r) + [0] * (width - len(r)) for r in rows]
+            if return_tensors == "pt":
+                import torch
+                return {"input_ids": torch.tensor(ids, dtype=torch.long).reshape(len(rows), width),
+                        "attention_mask": torch.tensor(mask, dtype=torch.long).reshape(len(rows), width)}
+            return {"input_ids": ids, "attention_mask": mask}
+        ids, offs = one(text)
+        out = {"input_ids": ids}
+        if return_offsets_mapping:
+            out["offset_mapping"] = offs
+        return out
+
+
 # Span mix used for the benchmark workloads: structure alone gives about 10-13%
 # causal block density at 12K-16K tokens (block 64, 4-block window, sink block,
 # 128-token groups), about 15-21% with the pooled top-8 blocks added.

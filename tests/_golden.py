@@ -53,3 +53,24 @@ def tokenizer(g):
 def bf16_bits_to_f32(a):
     import torch
     return torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16).float()
+
+
+def bf16_bits_to_np(a):
+    """uint16 bf16 bit patterns -> float32 numpy array."""
+    return (a.astype(np.uint32) << 16).view(np.float32)
+
+
+SIM_PARAM_KEYS = ("chunk_similarity_top_percent", "chunk_similarity_max_neighbors",
+                  "chunk_similarity_max_tokens_per_chunk")
+
+
+def sim_case(g, name):
+    """(texts, embedding fp32, params, src, tgt, edges) of a similarity.npz case."""
+    texts = [str(t) for t in g[f"{name}_texts"]]
+    emb = bf16_bits_to_np(g[f"{name}_emb_bf16"])
+    p = {k: g[f"{name}_p_{k}"].item() for k in SIM_PARAM_KEYS}
+    sub = bool(g[f"{name}_has_subsets"])
+    src = g[f"{name}_src"].tolist() if sub else None
+    tgt = g[f"{name}_tgt"].tolist() if sub else None
+    edges = deps(g, f"{name}_edge_src", f"{name}_edge_dst")
+    return texts, emb, p, src, tgt, edges

@@ -22,6 +22,11 @@ What is recorded (all from the reference's own code, unmodified):
 * ``attn_*.npz`` -- ``_fwd_kernel_sabrecoder`` (:28-116) run by Triton's
   interpreter in fp32 on bf16-representable inputs.
 * ``sparsity_utils.json`` -- utils/sparsity_utils.py values.
+* ``similarity.npz`` -- ``_similarity_edges`` (:581-682, with
+  ``_get_or_build_similarity_vectors`` :490-579 and ``_clean_for_similarity``
+  :458-472) on seeded chunk texts and a seeded bf16 embedding table, for
+  three parameter sets, and ``build_block_indices`` end to end with
+  ``use_chunk_similarity=True``.
 
 The tree-sitter modules (pinned tree-sitter==0.20.4,
 tree-sitter-languages==1.10.2 in the reference's requirements.txt) are
@@ -56,7 +61,8 @@ import sabrecoder_attention_triton as R  # noqa: E402
 from semantic_chunker import ChunkType, CodeChunk  # noqa: E402
 from utils import sparsity_utils as SU  # noqa: E402
 
-from sabrecoder_b200.spans import LineTokenizer, WordTokenizer, make_spans, spans_to_code  # noqa: E402
+from sabrecoder_b200.spans import (HashTokenizer, LineTokenizer, WordTokenizer, make_spans,  # noqa: E402
+                                   spans_to_code)
 
 _TYPE = {"import": ChunkType.IMPORT, "function": ChunkType.FUNCTION, "class": ChunkType.CLASS,
          "statement": ChunkType.MODULE_CODE}
@@ -222,6 +228,112 @@ def record_builder_full():
     print(f"builder_full: nb={nb} chunks {len(seg_chunks)} -> {len(filled)} edges={len(edges)}")
 
 
+def similarity_texts(seed, n_chunks=60):
+    """Chunk texts with shared and private identifiers, commented lines (the
+    cleaning rule), a blank chunk and a comment-marker-only chunk."""
+    rng = np.random.default_rng(seed)
+    shared = [f"w{i}" for i in range(40)]
+    texts = []
+    for c in range(n_chunks):
+        if c == 7:
+            texts.append("   \n  ")
+            continue
+        if c == 11:
+            texts.append("# \n// ")
+            continue
+        lines = []
+        for _ in range(int(rng.integers(1, 6))):
+            words = [shared[int(rng.integers(0, len(shared)))] for _ in range(int(rng.integers(1, 7)))]
+            words.append(f"p{c}_{int(rng.integers(0, 3))}")
+            pre = ["", "", "# ", "// ", "#"][int(rng.integers(0, 5))]
+            lines.append(pre + " ".join(words))
+        texts.append("\n".join(lines))
+    return texts
+
+
+def record_similarity():
+    """_similarity_edges for three parameter sets, and build_block_indices with
+    use_chunk_similarity=True end to end."""
+    tok = HashTokenizer(vocab=128)
+    out = {}
+
+    def bf16_bits(t):
+        return t.view(torch.int16).numpy().view(np.uint16)
+
+    cases = [("a", 0, 200, dict(chunk_similarity_top_percent=0.1, chunk_similarity_max_neighbors=8,
+                                 chunk_similarity_max_tokens_per_chunk=256), None, None),
+             ("b", 1, 256, dict(chunk_similarity_top_percent=25, chunk_similarity_max_neighbors=3,
+                                 chunk_similarity_max_tokens_per_chunk=5), None, None),
+             ("c", 2, 128, dict(chunk_similarity_top_percent=0.5, chunk_similarity_max_neighbors=4,
+                                 chunk_similarity_max_tokens_per_chunk=64), list(range(10, 60)), list(range(0, 10)))]
+    for name, seed, dim, params, src, tgt in cases:
+        texts = similarity_texts(100 + seed)
+        g = torch.Generator().manual_seed(200 + seed)
+        emb = torch.randn(128, dim, generator=g).to(torch.bfloat16)
+        chunks = [CodeChunk(ChunkType.MODULE_CODE, 0, 0, t, name=f"c{i}", start_line=i + 1, end_line=i + 1)
+                  for i, t in enumerate(texts)]
+        mb = R.StructureAwareMaskBuilder(tok, use_chunk_similarity=True, embedding_weight=emb, **params)
+        edges = mb._similarity_edges(chunks, f"code-{name}", src_indices=src, tgt_indices=tgt)
+        esrc, edst = deps_to_arrays(edges)
+        out.update({f"{name}_texts": np.asarray(texts), f"{name}_emb_bf16": bf16_bits(emb),
+                    f"{name}_src": np.asarray(src if src is not None else [], np.int32),
+                    f"{name}_tgt": np.asarray(tgt if tgt is not None else [], np.int32),
+                    f"{name}_has_subsets": np.asarray(src is not None),
+                    f"{name}_edge_src": esrc, f"{name}_edge_dst": edst,
+                    **{f"{name}_p_{k}": np.asarray(v) for k, v in params.items()}})
+        print(f"similarity {name}: dim={dim} chunks={len(texts)} edges={len(esrc)}")
+
+    # end to end: fixed segmenter/analyser, similarity edges merged into R2
+    L = 900
+    texts = similarity_texts(7, n_chunks=45)
+    lines, chunks = [], []
+    for i, t in enumerate(texts):
+        s0 = len(lines) + 1
+        body = t.split("\n")
+        lines.extend(body)
+        chunks.append(CodeChunk(ChunkType.FUNCTION if i % 4 == 0 else ChunkType.MODULE_CODE, 0, 0, t,
+                                name=f"c{i}", start_line=s0, end_line=len(lines),
+                                signature_start_line=s0 if i % 4 == 0 else None,
+                                signature_end_line=s0 if i % 4 == 0 else None))
+    code = "\n".join(lines)
+
+    class Seg:
+        def __init__(self, tokenizer=None):
+            pass
+
+        def segment_code(self, code, language=None):
+            return list(chunks)
+
+    class Ana:
+        def __init__(self, chunks, code, language=None):
+            pass
+
+        def analyze(self):
+            return [_Ref(4, 0)]
+
+    R.TreeSitterSegmenter, R.CrossReferenceAnalyzer = Seg, Ana
+    g = torch.Generator().manual_seed(300)
+    emb = torch.randn(128, 256, generator=g).to(torch.bfloat16)
+    params = dict(window_size=64, num_prefix_tokens=16, num_suffix_tokens=32, block_size=16,
+                  global_last_k_chunks=1, max_chunk_tokens=0)
+    sim = dict(chunk_similarity_top_percent=0.1, chunk_similarity_max_neighbors=8,
+               chunk_similarity_max_tokens_per_chunk=256)
+    mb = R.StructureAwareMaskBuilder(tok, use_chunk_similarity=True, embedding_weight=emb, **params, **sim)
+    bi, bc, bm = mb.build_block_indices(code, L, torch.device("cpu"))
+    nb = bm.shape[0]
+    canon = np.full(bi.shape, -1, np.int32)
+    for r in range(nb):
+        c = int(bc[0, r])
+        canon[0, r, :c] = np.sort(bi[0, r, :c].numpy())
+    out.update({"e2e_code": np.asarray(code), "e2e_seq_len": L, "e2e_emb_bf16": bf16_bits(emb),
+                **{f"e2e_p_{k}": np.asarray(v) for k, v in {**params, **sim}.items()},
+                **{f"e2e_{k}": v for k, v in chunk_arrays(chunks).items()},
+                "e2e_texts": np.asarray(texts), "e2e_block_mask": bm.numpy().astype(np.uint8),
+                "e2e_block_counts": bc.numpy(), "e2e_indices_sorted": canon})
+    np.savez_compressed(os.path.join(HERE, "similarity.npz"), **out)
+    print(f"similarity e2e: nb={nb} density={float(bm.sum()) / (nb * (nb + 1) / 2):.3f}")
+
+
 def record_attention(name, B, H, L, D, block, seed):
     g = torch.Generator().manual_seed(seed)
     q, k, v = [torch.randn(B, H, L, D, generator=g).to(torch.bfloat16).float() for _ in range(3)]
@@ -314,6 +426,7 @@ def main():
     record_attention("b64", B=2, H=1, L=200, D=128, block=64, seed=21)
     record_attention("b128", B=1, H=1, L=300, D=128, block=128, seed=22)
     record_sparsity_utils()
+    record_similarity()
 
 
 if __name__ == "__main__":

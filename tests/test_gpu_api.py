@@ -246,3 +246,99 @@ def test_sabre_kv_cache_generate_matches_dynamic_cache(cuda, topk):
     for sa, sb in zip(a.scores, b.scores):
         assert torch.equal(sa, sb)
     assert cache.get_seq_length() == L + 11
+
+
+# ---------------------------------------------------------------------------
+# chunk-similarity edges
+# ---------------------------------------------------------------------------
+
+def _sim_builder(emb, p, **mask_params):
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder, clear_all_caches
+    from sabrecoder_b200.spans import HashTokenizer
+    clear_all_caches()
+    return StructureAwareMaskBuilder(HashTokenizer(128), use_chunk_similarity=True,
+                                     embedding_weight=torch.from_numpy(emb).to(torch.bfloat16), **p, **mask_params)
+
+
+@pytest.mark.parametrize("name", ["a", "b", "c"])
+def test_chunk_vectors_and_topk_bit_exact_vs_oracle(cuda, name):
+    """sabre_chunk_vectors and sabre_similarity_topk equal the oracle's
+    fixed-order restatement bit for bit."""
+    from sabrecoder_b200 import kernels as K
+    from sabrecoder_b200.spans import HashTokenizer
+    g = G.load("similarity.npz")
+    texts, emb, p, src, tgt, _ = G.sim_case(g, name)
+    tok = HashTokenizer(128)
+    cleaned = [MO.clean_for_similarity(t) for t in texts]
+    keep = [i for i, t in enumerate(cleaned) if t.strip()]
+    lists = MO.tokenize_for_similarity(tok, [cleaned[i] for i in keep], p["chunk_similarity_max_tokens_per_chunk"])
+    want = MO.chunk_vectors_f16(emb, lists)
+    ptr = np.zeros(len(lists) + 1, np.int32)
+    ptr[1:] = np.cumsum([len(x) for x in lists])
+    flat = np.asarray([t for x in lists for t in x], np.int32)
+    emb_d = torch.from_numpy(emb).to(torch.bfloat16).cuda()
+    got = K.chunk_vectors(emb_d, torch.from_numpy(ptr).cuda(), torch.from_numpy(flat).cuda())
+    np.testing.assert_array_equal(got.cpu().numpy().view(np.uint16), want.view(np.uint16))
+    rows = list(range(len(keep)))
+    s_rows, t_rows = rows[: len(rows) // 2 + 3], rows[2:]
+    k = 5
+    want_t = MO.similarity_topk(want, s_rows, [keep[r] for r in s_rows], t_rows, [keep[r] for r in t_rows], k)
+
+    def i32(x):
+        return torch.tensor(x, dtype=torch.int32, device="cuda")
+
+    got_t = K.similarity_topk(got, i32(s_rows), i32([keep[r] for r in s_rows]), i32(t_rows),
+                              i32([keep[r] for r in t_rows]), k)
+    np.testing.assert_array_equal(got_t.cpu().numpy(), np.asarray(want_t, np.int32))
+
+
+@pytest.mark.parametrize("name", ["a", "b", "c"])
+def test_builder_similarity_edges_match_reference(cuda, name):
+    from sabrecoder_b200.chunks import ChunkType, CodeChunk
+    g = G.load("similarity.npz")
+    texts, emb, p, src, tgt, want = G.sim_case(g, name)
+    mb = _sim_builder(emb, p)
+    chunks = [CodeChunk(ChunkType.MODULE_CODE, 0, 0, t, name=f"c{i}", start_line=i + 1, end_line=i + 1)
+              for i, t in enumerate(texts)]
+    got = mb._similarity_edges(chunks, f"code-{name}", src_indices=src, tgt_indices=tgt)
+    assert got == want
+
+
+def test_build_block_indices_with_similarity_matches_reference(cuda):
+    """build_block_indices with use_chunk_similarity=True end to end (fixed
+    segmenter/analyser) equals the reference's mask and index lists."""
+    from sabrecoder_b200.chunks import ChunkType, CodeChunk
+    g = G.load("similarity.npz")
+    texts = [str(t) for t in g["e2e_texts"]]
+    spec = G.chunks(g, "e2e_")
+    chunks = [CodeChunk(ChunkType.FUNCTION if s.chunk_type.name == "FUNCTION" else ChunkType.MODULE_CODE, 0, 0, t,
+                        name=s.name, start_line=s.start_line, end_line=s.end_line,
+                        signature_start_line=s.signature_start_line, signature_end_line=s.signature_end_line)
+              for s, t in zip(spec, texts)]
+
+    class Seg:
+        def __init__(self, tokenizer=None):
+            pass
+
+        def segment_code(self, code, language=None):
+            return list(chunks)
+
+    class Ref:
+        source_chunk_idx, target_chunk_idx = 4, 0
+
+    class Ana:
+        def __init__(self, chunks, code, language=None):
+            pass
+
+        def analyze(self):
+            return [Ref()]
+
+    p = {k: g[f"e2e_p_{k}"].item() for k in G.SIM_PARAM_KEYS}
+    mp = {k: int(g[f"e2e_p_{k}"]) for k in ("window_size", "num_prefix_tokens", "num_suffix_tokens", "block_size",
+                                          "global_last_k_chunks", "max_chunk_tokens")}
+    mb = _sim_builder(G.bf16_bits_to_np(g["e2e_emb_bf16"]), p, **mp)
+    mb.segmenter_factory, mb.analyzer_factory = Seg, Ana
+    bi, bc, bm = mb.build_block_indices(str(g["e2e_code"]), int(g["e2e_seq_len"]), cuda)
+    np.testing.assert_array_equal(bm.cpu().numpy(), g["e2e_block_mask"])
+    np.testing.assert_array_equal(bc.cpu().numpy(), g["e2e_block_counts"])
+    np.testing.assert_array_equal(bi.cpu().numpy(), g["e2e_indices_sorted"])

@@ -124,3 +124,57 @@ def test_topk_extension_properties():
                 worst_in = sc[h, qb][added].min()
                 out = [c for c in cand if not added[c]]
                 assert all(sc[h, qb, c] <= worst_in for c in out)
+
+
+@pytest.mark.parametrize("name", ["a", "b", "c"])
+def test_similarity_edges_oracle_matches_reference(name):
+    """The oracle's chunk-similarity edges equal the reference's
+    _similarity_edges on seeded texts and a bf16 embedding table (fraction and
+    percent top_percent, truncation to 5 tokens, source/target subsets, a
+    blank chunk and a comment-marker-only chunk)."""
+    from sabrecoder_b200.spans import HashTokenizer
+    g = G.load("similarity.npz")
+    texts, emb, p, src, tgt, want = G.sim_case(g, name)
+    got = MO.similarity_edges(texts, HashTokenizer(128), emb, top_percent=p["chunk_similarity_top_percent"],
+                              max_tokens=p["chunk_similarity_max_tokens_per_chunk"],
+                              max_neighbors=p["chunk_similarity_max_neighbors"], src_indices=src, tgt_indices=tgt)
+    assert got == want
+
+
+def test_similarity_builder_end_to_end_oracle_matches_reference():
+    from sabrecoder_b200.spans import HashTokenizer
+    g = G.load("similarity.npz")
+    chunks = G.chunks(g, "e2e_")
+    texts = [str(t) for t in g["e2e_texts"]]
+    for c, t in zip(chunks, texts):
+        c.text = t
+    emb = G.bf16_bits_to_np(g["e2e_emb_bf16"])
+    deps = {4: {0}, 0: {4}}
+    sim = MO.similarity_edges(texts, HashTokenizer(128), emb,
+                              top_percent=g["e2e_p_chunk_similarity_top_percent"].item(),
+                              max_tokens=int(g["e2e_p_chunk_similarity_max_tokens_per_chunk"]),
+                              max_neighbors=int(g["e2e_p_chunk_similarity_max_neighbors"]))
+    for s_, t_ in sim.items():
+        deps.setdefault(s_, set()).update(t_)
+    mp = {k: int(g[f"e2e_p_{k}"]) for k in ("window_size", "num_prefix_tokens", "num_suffix_tokens", "block_size",
+                                          "global_last_k_chunks", "max_chunk_tokens")}
+    m = MO.build_block_mask_from_chunks(code=str(g["e2e_code"]), seq_len=int(g["e2e_seq_len"]), chunks=chunks,
+                                        chunk_deps=deps, import_chunks=set(), language=None,
+                                        tokenizer=HashTokenizer(128), **mp)
+    np.testing.assert_array_equal(m, g["e2e_block_mask"])
+
+
+def test_similarity_reduction_orders_are_fixed():
+    """chunk_vectors_f16 / similarity_scores follow their documented orders:
+    a shuffled summation gives different low bits somewhere, the documented
+    one is reproducible."""
+    rng = np.random.default_rng(5)
+    emb = rng.standard_normal((50, 300)).astype(np.float32)
+    v1 = MO.chunk_vectors_f16(emb, [[1, 2, 3], [], [4]])
+    v2 = MO.chunk_vectors_f16(emb, [[1, 2, 3], [], [4]])
+    np.testing.assert_array_equal(v1, v2)
+    assert not v1[1].any()  # an empty chunk is the zero vector
+    n = np.linalg.norm(v1[0].astype(np.float64))
+    assert abs(n - 1.0) < 2e-3
+    sc = MO.similarity_scores(v1[0], v1)
+    assert abs(sc[0] - 1.0) < 5e-3 and sc[1] == 0.0
