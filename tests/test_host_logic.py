@@ -75,3 +75,33 @@ def test_map_tokens_last_chunk_wins_and_negative_lines():
     got = mb._map_tokens_to_chunks(code, chunks, 12)
     want = MO.map_tokens_to_chunks(code, chunks, LineTokenizer(), 12).tolist()
     assert got == want
+
+
+def test_precomputed_blocks_round_trip_and_reference_format(tmp_path):
+    """Files in the reference evaluator's format ({idx: (indices, counts)},
+    torch.save) load, including its int64 unordered rows, and files written
+    here load back unchanged."""
+    import torch
+    from sabrecoder_b200.precomputed import load_precomputed_blocks, precompute_blocks, save_precomputed_blocks
+    g = G.load("builder_full.npz")
+    raw = torch.from_numpy(g["raw_indices"]).long()      # reference rows: unordered, padded with -1
+    cnt = torch.from_numpy(g["block_counts"]).long()
+    ref_file = tmp_path / "ref.pt"
+    torch.save({0: (raw[:1].clone(), cnt[:1].clone()), 3: (raw[1:].clone(), cnt[1:].clone())}, ref_file)
+    got = load_precomputed_blocks(str(ref_file))
+    assert sorted(got) == [0, 3]
+    assert got[0][0].dtype == torch.int32 and got[0][1].dtype == torch.int32
+    assert torch.equal(got[3][0], raw[1:].int()) and torch.equal(got[3][1], cnt[1:].int())
+    ours = tmp_path / "ours.pt"
+    save_precomputed_blocks(str(ours), got)
+    back = torch.load(ours, weights_only=True)
+    assert sorted(back) == [0, 3] and torch.equal(back[0][0], got[0][0])
+    built = precompute_blocks(lambda i, s: (s[0], s[1], None), [(5, (raw[:1].int(), cnt[:1].int()))])
+    assert list(built) == [5] and torch.equal(built[5][0], raw[:1].int())
+    bad = tmp_path / "bad.pt"
+    torch.save({1: (raw[0, 0], cnt)}, bad)
+    with pytest.raises(ValueError):
+        load_precomputed_blocks(str(bad))
+    torch.save({1: (raw.float(), cnt)}, bad)
+    with pytest.raises(TypeError):
+        load_precomputed_blocks(str(bad))
