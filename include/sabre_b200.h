@@ -249,6 +249,45 @@ int sabre_similarity_topk(const void* vecs_f16, int dim, const int32_t* src_rows
                           int nsrc, const int32_t* tgt_rows, const int32_t* tgt_chunk, int ntgt, int k,
                           int32_t* out_tgt_chunk, void* stream);
 
+/* ----------------------------------------------------------------------
+ * (3e) Token-level sparsity (the reference's use_token_level_sparsity=True:
+ * build_token_level_mask / _build_mask_from_chunks,
+ * sabrecoder_attention_triton.py:1171-1454, compute_block_mask_from_token_mask
+ * :1862-1885 and _fwd_kernel_sabrecoder_token_sparse :119-215), block size 64,
+ * without an L x L mask.
+ *
+ * Per token t < seq_len: tok_chunk[t] (chunk id, -1 if none), tok_group[t]
+ * (chunk id, or chunk id combined with the max_chunk_tokens group), tok_global[t]
+ * (1 = visible to every query: import chunk, signature / special line,
+ * prefix, suffix, last-k chunk); dep_bits [nchunks][ceil(nchunks/32)]: bit t
+ * of row s set when chunk t is a dependency of chunk s. Key j is visible to
+ * query i when j <= i and (i - j <= window, tok_global[j], both chunks >= 0
+ * with equal groups, or both chunks >= 0 with chunk(j) a dependency of chunk(i)).
+ *
+ * sabre_token_block_mask: row_bits uint32 [nb][ceil(nb/32)] (nb = ceil(L/64)):
+ *   bit kb of row qb when any pair of query block qb and key block kb is
+ *   visible (the reference's block mask from the token mask).
+ * sabre_token_tile_masks: for every listed pair (indices [nb][cap] ascending,
+ *   counts [nb], row_ptr [nb] = exclusive prefix sum of counts) the 64 query
+ *   rows' 64-bit key masks at masks[(row_ptr[qb] + i) * 64 + row].
+ * sabre_prefill_bsa_tokenmask: sabre_prefill_bsa (block_size 64) that also
+ *   masks each element of a listed block by its tile mask. Lists must be
+ *   the ascending lists the masks were written for, shared by all batch
+ *   entries and heads (index/count strides as in sabre_prefill_bsa).
+ * ---------------------------------------------------------------------- */
+int sabre_token_block_mask(const int32_t* tok_chunk, const int32_t* tok_group, const uint8_t* tok_global,
+                           const uint32_t* dep_bits, int nchunks, int seq_len, int window, uint32_t* row_bits,
+                           void* stream);
+int sabre_token_tile_masks(const int32_t* tok_chunk, const int32_t* tok_group, const uint8_t* tok_global,
+                           const uint32_t* dep_bits, int nchunks, int seq_len, int window, const int32_t* indices,
+                           int cap, const int32_t* counts, const int32_t* row_ptr, uint64_t* masks, void* stream);
+int sabre_prefill_bsa_tokenmask(const void* q, const void* k, const void* v, void* o, const int32_t* block_indices,
+                                const int32_t* block_counts, const uint64_t* tile_masks,
+                                const int32_t* tile_row_ptr, int batch, int heads_q, int heads_kv, int seq_len,
+                                int head_dim, int max_active, const int64_t* q_strides, const int64_t* k_strides,
+                                const int64_t* v_strides, const int64_t* o_strides, const int64_t* idx_strides,
+                                const int64_t* cnt_strides, float softmax_scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

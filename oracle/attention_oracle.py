@@ -134,3 +134,22 @@ def dense_masked_sdpa(q, k, v, block_mask_2d, block_size: int) -> torch.Tensor:
         k = k.repeat_interleave(g, dim=1)
         v = v.repeat_interleave(g, dim=1)
     return torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=allowed)
+
+
+def token_masked_prefill_fp32(q, k, v, visible) -> torch.Tensor:
+    """Attention restricted to a token-level visibility matrix ``[L, L]`` (the
+    reference's token-level kernel, sabrecoder_attention_triton.py:119-215),
+    in fp32 with P rounded to the input dtype; rows with nothing visible give 0."""
+    B, H, L, D = q.shape
+    g = H // k.shape[1]
+    kf = k.float().repeat_interleave(g, dim=1)
+    vf = v.float().repeat_interleave(g, dim=1)
+    s = torch.matmul(q.float(), kf.transpose(-1, -2)) / (D ** 0.5)
+    vis = torch.as_tensor(visible, dtype=torch.bool)
+    s = s.masked_fill(~vis, float("-inf"))
+    m = s.amax(-1, keepdim=True)
+    m = torch.where(torch.isinf(m), torch.zeros_like(m), m)
+    p = torch.exp(s - m)
+    l = p.sum(-1, keepdim=True)
+    o = torch.matmul(p.to(q.dtype).float(), vf)
+    return torch.where(l > 0, o / l.clamp_min(1e-30), torch.zeros_like(o))

@@ -527,3 +527,81 @@ def similarity_edges(chunk_texts, tokenizer, embedding, *, top_percent: float, m
             if t >= 0:
                 edges.setdefault(int(c), set()).add(int(t))
     return edges
+
+
+# ---------------------------------------------------------------------------
+# Token-level mask (sabrecoder_attention_triton.py:1171-1266) and its block
+# mask (compute_block_mask_from_token_mask :1862-1885). Dense bool [L, L]:
+# only for the small sizes the tests use.
+# ---------------------------------------------------------------------------
+
+def token_level_mask_tokens(token_to_chunk: np.ndarray, nchunks: int, import_chunks, chunk_deps,
+                            global_token_mask: Optional[np.ndarray], *, seq_len: int, block_size: int,
+                            window_size: int, num_prefix_tokens: int, num_suffix_tokens: int,
+                            max_chunk_tokens: int, global_last_k_chunks: int) -> np.ndarray:
+    """``visible[i, j]`` following the reference's steps in order: sliding
+    window, same chunk (or same max_chunk_tokens group), chunk dependencies,
+    import chunks, signature/special lines, prefix, suffix, last-k chunks,
+    then causality."""
+    L = int(seq_len)
+    t2c = np.asarray(token_to_chunk, dtype=np.int64)[:L]
+    pos = np.arange(L)
+    dist = pos[:, None] - pos[None, :]
+    m = (dist >= 0) & (dist <= int(window_size))
+    ci, cj = t2c[:, None], t2c[None, :]
+    if max_chunk_tokens > 0:
+        bpg = max(1, int(max_chunk_tokens) // int(block_size))
+        gidx = (pos // int(block_size)) // bpg
+        ng = int(gidx.max()) + 2
+        gid = t2c * ng + gidx
+        m |= (gid[:, None] == gid[None, :]) & (ci != -1) & (cj != -1)
+    else:
+        m |= (ci == cj) & (ci != -1)
+    for s, tg in (chunk_deps or {}).items():
+        if not (0 <= int(s) < nchunks):
+            continue
+        src = t2c == int(s)
+        if not src.any():
+            continue
+        tgt = np.zeros(L, dtype=bool)
+        for t in tg:
+            if 0 <= int(t) < nchunks:
+                tgt |= t2c == int(t)
+        m |= src[:, None] & tgt[None, :]
+    for c in import_chunks or ():
+        m[:, t2c == int(c)] = True
+    if global_token_mask is not None:
+        m[:, np.asarray(global_token_mask, dtype=bool)[:L]] = True
+    npre = min(int(num_prefix_tokens), L)
+    if npre > 0:
+        m[:, :npre] = True
+    nsuf = min(int(num_suffix_tokens), L)
+    if nsuf > 0:
+        m[:, max(0, L - nsuf):] = True
+    k = int(global_last_k_chunks)
+    if k > 0 and nchunks > 0:
+        for c in range(max(0, nchunks - k), nchunks):
+            m[:, t2c == c] = True
+    return m & (dist >= 0)
+
+
+def token_level_mask_from_chunks(*, code: str, seq_len: int, chunks: Sequence, chunk_deps, import_chunks,
+                                 language: Optional[str], tokenizer, block_size: int, window_size: int,
+                                 num_prefix_tokens: int, num_suffix_tokens: int, max_chunk_tokens: int,
+                                 global_last_k_chunks: int) -> np.ndarray:
+    """Whole of ``_build_mask_from_chunks`` as a bool visibility matrix."""
+    t2c = map_tokens_to_chunks(code, chunks, tokenizer, seq_len)
+    gtm = global_token_mask_from_chunks(code, chunks, tokenizer, seq_len, language)
+    return token_level_mask_tokens(t2c, len(chunks), import_chunks, chunk_deps, gtm, seq_len=seq_len,
+                                   block_size=block_size, window_size=window_size,
+                                   num_prefix_tokens=num_prefix_tokens, num_suffix_tokens=num_suffix_tokens,
+                                   max_chunk_tokens=max_chunk_tokens, global_last_k_chunks=global_last_k_chunks)
+
+
+def block_mask_from_token_mask(visible: np.ndarray, block: int) -> np.ndarray:
+    """Block (i, j) is listed iff any of its token pairs is visible."""
+    L = visible.shape[0]
+    nb = (L + block - 1) // block
+    pad = np.zeros((nb * block, nb * block), dtype=bool)
+    pad[:L, :L] = visible
+    return pad.reshape(nb, block, nb, block).any(axis=(1, 3))

@@ -44,6 +44,10 @@ SIGNATURES = {
                                   c_size_t, P]),
     "sabre_chunk_vectors": (c_int, [P, c_int, c_int, c_int, P, P, c_int, P, P]),
     "sabre_similarity_topk": (c_int, [P, c_int, P, P, c_int, P, P, c_int, c_int, P, P]),
+    "sabre_token_block_mask": (c_int, [P, P, P, P, c_int, c_int, c_int, P, P]),
+    "sabre_token_tile_masks": (c_int, [P, P, P, P, c_int, c_int, c_int, P, c_int, P, P, P, P]),
+    "sabre_prefill_bsa_tokenmask": (c_int, [P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
+                                            I64P, I64P, I64P, I64P, I64P, I64P, c_float, c_int, P]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

@@ -80,6 +80,10 @@ constexpr uint32_t kTmemS = 128;
 constexpr uint32_t kTmemP = 192;  // + 32 * buffer
 
 struct Params {
+  // Token-level variant only (block size 64): the 64-bit row masks of every
+  // listed (query block, key block) pair, in list order from tmask_ptr[qb].
+  const unsigned long long* tmask;
+  const int32_t* tmask_ptr;
   void* o;                      // output rows, written with 16-byte stores
   long long o_sb, o_sh, o_sl;   // element strides (d stride 1)
   const int32_t* idx;
@@ -110,7 +114,8 @@ struct UnionIter {
   }
 };
 
-template <typename T>
+// kTok: also apply the token-level masks of the listed blocks (Params::tmask).
+template <typename T, bool kTok>
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_bsa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -283,9 +288,25 @@ __global__ void __launch_bounds__(kThreads, 2)
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = start_ok;
+    // Token-level variant: this half's listed tiles come in ascending order,
+    // so a tile's position in its (ascending) list is a running count.
+    int rank = 0;
+    const bool trow = kTok && (r0 + half * 64) < p.L;
+    const long long tbase = trow ? p.tmask_ptr[(r0 + half * 64) / 64] : 0;
+    // Reads never pass this row's own masks, even for lists other than the
+    // ones the masks were written for (a missing mask hides the whole tile).
+    const int tcount = trow ? min(p.cnt[b * p.cnt_sb + h * p.cnt_sh + ((r0 + half * 64) / 64) * p.cnt_sm],
+                                  p.max_active) : 0;
     UnionIter it(bits, bits + kWords, nw);
     for (int j = 0; ok && j < n; ++j) {
       const int kt = it.next();
+      const bool vis = (bits[half * kWords + (kt >> 5)] >> (kt & 31)) & 1u;
+      unsigned long long tw = ~0ull;
+      if constexpr (kTok) {
+        // issued before the S wait so the load overlaps it
+        tw = (vis && rank < tcount) ? p.tmask[(tbase + rank) * 64 + (row & 63)] : 0ull;
+        rank += vis ? 1 : 0;
+      }
       ok = mbar_wait_warp(bar(S_FULL + j % kKStages), (j / kKStages) & 1, abort_flag);
       if (!ok) break;
       tc_fence_after();
@@ -297,7 +318,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(S_EMPTY));
 
-      const bool vis = (bits[half * kWords + (kt >> 5)] >> (kt & 31)) & 1u;
       const int nvalid = vis ? min(64, max(0, r_abs - kt * 64 + 1)) : 0;
       float x[64];
 #pragma unroll
@@ -305,10 +325,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         x[c] = __uint_as_float(sr0[c]);
         x[c + 32] = __uint_as_float(sr1[c]);
       }
-      if (nvalid < 64) {
+      if (nvalid < 64 || (kTok && tw != ~0ull)) {
 #pragma unroll
         for (int c = 0; c < 64; ++c)
-          if (c >= nvalid) x[c] = -INFINITY;
+          if (c >= nvalid || !((tw >> c) & 1ull)) x[c] = -INFINITY;
       }
       // Row max as 8 independent chains, then a tree (short dependency chain).
       float m8[8];

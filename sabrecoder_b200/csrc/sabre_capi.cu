@@ -15,6 +15,7 @@
 #include "rope_cache.cu"
 #include "topk.cu"
 #include "similarity.cu"
+#include "token_mask.cu"
 
 #define SABRE_VERSION 100
 
@@ -128,12 +129,16 @@ int sabre_device_status(unsigned int* flags_out, int clear, void* stream) {
   return SABRE_OK;
 }
 
-int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, const int32_t* block_indices,
-                      const int32_t* block_counts, int batch, int heads_q, int heads_kv, int seq_len,
-                      int head_dim, int block_size, int max_active, const int64_t* q_strides,
-                      const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
-                      const int64_t* idx_strides, const int64_t* cnt_strides, float softmax_scale, int dtype,
-                      void* stream) {
+}  // extern "C"
+
+namespace sabre {
+// Shared by sabre_prefill_bsa and sabre_prefill_bsa_tokenmask (tmask != null).
+static int prefill_launch(const void* q, const void* k, const void* v, void* o, const int32_t* block_indices,
+                          const int32_t* block_counts, int batch, int heads_q, int heads_kv, int seq_len,
+                          int head_dim, int block_size, int max_active, const int64_t* q_strides,
+                          const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                          const int64_t* idx_strides, const int64_t* cnt_strides, float softmax_scale, int dtype,
+                          const uint64_t* tmask, const int32_t* tmask_ptr, void* stream) {
   using namespace sabre::prefill;
   if (!q || !k || !v || !o || !block_indices || !block_counts || !q_strides || !k_strides || !v_strides ||
       !o_strides || !idx_strides || !cnt_strides)
@@ -171,6 +176,8 @@ int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, cons
     return st;
 
   Params p;
+  p.tmask = reinterpret_cast<const unsigned long long*>(tmask);
+  p.tmask_ptr = tmask_ptr;
   p.o = o;
   p.o_sb = o_strides[0];
   p.o_sh = o_strides[1];
@@ -199,15 +206,50 @@ int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, cons
     return fail(SABRE_ERR_UNSUPPORTED, "sabre_prefill_bsa: grid too large");
   dim3 grid(batch * heads_q, p.ntiles);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == SABRE_BF16) {
-    if ((st = ensure_smem_attr(prefill_bsa_kernel<__nv_bfloat16>, kSmemBytes)) != SABRE_OK) return st;
-    prefill_bsa_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
+  const bool tok = (tmask != nullptr);
+  if (dtype == SABRE_BF16 && !tok) {
+    if ((st = ensure_smem_attr(prefill_bsa_kernel<__nv_bfloat16, false>, kSmemBytes)) != SABRE_OK) return st;
+    prefill_bsa_kernel<__nv_bfloat16, false><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
+  } else if (dtype == SABRE_BF16) {
+    if ((st = ensure_smem_attr(prefill_bsa_kernel<__nv_bfloat16, true>, kSmemBytes)) != SABRE_OK) return st;
+    prefill_bsa_kernel<__nv_bfloat16, true><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
+  } else if (!tok) {
+    if ((st = ensure_smem_attr(prefill_bsa_kernel<__half, false>, kSmemBytes)) != SABRE_OK) return st;
+    prefill_bsa_kernel<__half, false><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
   } else {
-    if ((st = ensure_smem_attr(prefill_bsa_kernel<__half>, kSmemBytes)) != SABRE_OK) return st;
-    prefill_bsa_kernel<__half><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
+    if ((st = ensure_smem_attr(prefill_bsa_kernel<__half, true>, kSmemBytes)) != SABRE_OK) return st;
+    prefill_bsa_kernel<__half, true><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
   }
   SABRE_CUDA_TRY(cudaGetLastError());
   return SABRE_OK;
+}
+
+}  // namespace sabre
+
+extern "C" {
+
+int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, const int32_t* block_indices,
+                      const int32_t* block_counts, int batch, int heads_q, int heads_kv, int seq_len,
+                      int head_dim, int block_size, int max_active, const int64_t* q_strides,
+                      const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                      const int64_t* idx_strides, const int64_t* cnt_strides, float softmax_scale, int dtype,
+                      void* stream) {
+  return sabre::prefill_launch(q, k, v, o, block_indices, block_counts, batch, heads_q, heads_kv, seq_len, head_dim,
+                               block_size, max_active, q_strides, k_strides, v_strides, o_strides, idx_strides,
+                               cnt_strides, softmax_scale, dtype, nullptr, nullptr, stream);
+}
+
+int sabre_prefill_bsa_tokenmask(const void* q, const void* k, const void* v, void* o, const int32_t* block_indices,
+                                const int32_t* block_counts, const uint64_t* tile_masks,
+                                const int32_t* tile_row_ptr, int batch, int heads_q, int heads_kv, int seq_len,
+                                int head_dim, int max_active, const int64_t* q_strides, const int64_t* k_strides,
+                                const int64_t* v_strides, const int64_t* o_strides, const int64_t* idx_strides,
+                                const int64_t* cnt_strides, float softmax_scale, int dtype, void* stream) {
+  if (!tile_masks || !tile_row_ptr)
+    return sabre::fail(SABRE_ERR_INVALID_ARG, "sabre_prefill_bsa_tokenmask: null tile masks");
+  return sabre::prefill_launch(q, k, v, o, block_indices, block_counts, batch, heads_q, heads_kv, seq_len, head_dim,
+                               64, max_active, q_strides, k_strides, v_strides, o_strides, idx_strides, cnt_strides,
+                               softmax_scale, dtype, tile_masks, tile_row_ptr, stream);
 }
 
 }  // extern "C"

@@ -56,14 +56,20 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 def prefill_bsa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_indices: torch.Tensor,
                 block_counts: torch.Tensor, block_size: int, softmax_scale: Optional[float] = None,
-                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                out: Optional[torch.Tensor] = None, token_masks=None) -> torch.Tensor:
     """Block-sparse causal attention.
 
     q: ``[B, Hq, L, D]``; k, v: ``[B, Hkv, L, D]`` (any strides with unit
     head-dim stride, 16-byte aligned); block_indices ``[B, nb, max]`` (shared
     by heads, the reference layout) or ``[B, Hq, nb, max]``; block_counts
-    ``[B, nb]`` or ``[B, Hq, nb]``. Returns ``[B, Hq, L, D]`` in q's dtype."""
+    ``[B, nb]`` or ``[B, Hq, nb]``. Returns ``[B, Hq, L, D]`` in q's dtype.
+
+    ``token_masks=(tile_masks, row_ptr)`` (from :func:`token_tile_masks`,
+    block size 64) also masks every element of a listed block: the
+    token-level variant."""
     _need_cuda(q=q, k=k, v=v, block_indices=block_indices, block_counts=block_counts)
+    if token_masks is not None and int(block_size) != 64:
+        raise SabreError("the token-level variant needs block_size 64")
     if q.dtype not in DTYPE_CODE or k.dtype != q.dtype or v.dtype != q.dtype:
         raise SabreError(f"q/k/v must share dtype bf16 or f16 (got {q.dtype}, {k.dtype}, {v.dtype})")
     B, Hq, L, D = q.shape
@@ -91,11 +97,23 @@ def prefill_bsa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_indices
     if PREFILL_EVENTS is not None:
         ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
         ev[0].record(torch.cuda.current_stream(q.device))
-    st = lib().sabre_prefill_bsa(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), bi.data_ptr(), bc.data_ptr(), B, Hq, Hkv, L, D,
-        int(block_size), int(bi.shape[-1]), i64(q.stride()), i64(k.stride()), i64(v.stride()), i64(out.stride()),
-        i64(idx_strides), i64(cnt_strides), float(softmax_scale or 0.0), DTYPE_CODE[q.dtype], _stream(q))
-    check(st, "sabre_prefill_bsa")
+    if token_masks is None:
+        st = lib().sabre_prefill_bsa(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), bi.data_ptr(), bc.data_ptr(), B, Hq, Hkv, L,
+            D, int(block_size), int(bi.shape[-1]), i64(q.stride()), i64(k.stride()), i64(v.stride()),
+            i64(out.stride()), i64(idx_strides), i64(cnt_strides), float(softmax_scale or 0.0), DTYPE_CODE[q.dtype],
+            _stream(q))
+        check(st, "sabre_prefill_bsa")
+    else:
+        tm, rp = token_masks
+        _need_cuda(tile_masks=tm, row_ptr=rp)
+        _i32(rp, "row_ptr")
+        st = lib().sabre_prefill_bsa_tokenmask(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), bi.data_ptr(), bc.data_ptr(), tm.data_ptr(),
+            rp.data_ptr(), B, Hq, Hkv, L, D, int(bi.shape[-1]), i64(q.stride()), i64(k.stride()), i64(v.stride()),
+            i64(out.stride()), i64(idx_strides), i64(cnt_strides), float(softmax_scale or 0.0), DTYPE_CODE[q.dtype],
+            _stream(q))
+        check(st, "sabre_prefill_bsa_tokenmask")
     LAUNCHES[0] += 1
     if ev is not None:
         ev[1].record(torch.cuda.current_stream(q.device))
@@ -359,3 +377,47 @@ def similarity_topk(vecs: torch.Tensor, src_rows: torch.Tensor, src_chunk: torch
     check(st, "sabre_similarity_topk")
     LAUNCHES[0] += 1
     return out
+
+
+# ---------------------------------------------------------------------------
+# (3e) token-level sparsity
+# ---------------------------------------------------------------------------
+
+def token_block_mask(tok_chunk: torch.Tensor, tok_group: torch.Tensor, tok_global: torch.Tensor,
+                     dep_bits: torch.Tensor, nchunks: int, window: int) -> torch.Tensor:
+    """uint32-as-int32 ``[nb, ceil(nb/32)]`` row bitsets of the blocks (64)
+    holding any visible token pair (sabre_token_block_mask)."""
+    _need_cuda(tok_chunk=tok_chunk, tok_group=tok_group, tok_global=tok_global, dep_bits=dep_bits)
+    L = tok_chunk.numel()
+    nb = (L + 63) // 64
+    bits = torch.empty(nb, (nb + 31) // 32, dtype=torch.int32, device=tok_chunk.device)
+    st = lib().sabre_token_block_mask(tok_chunk.data_ptr(), tok_group.data_ptr(), tok_global.data_ptr(),
+                                      dep_bits.data_ptr() if dep_bits.numel() else None, int(nchunks), L, int(window),
+                                      bits.data_ptr(), _stream(tok_chunk))
+    check(st, "sabre_token_block_mask")
+    LAUNCHES[0] += 1
+    return bits
+
+
+def token_tile_masks(tok_chunk: torch.Tensor, tok_group: torch.Tensor, tok_global: torch.Tensor,
+                     dep_bits: torch.Tensor, nchunks: int, window: int, indices: torch.Tensor,
+                     counts: torch.Tensor):
+    """``(tile_masks int64 [total, 64], row_ptr int32 [nb])``: the 64-bit key
+    masks of the 64 query rows of every listed (query block, key block) pair,
+    in list order (sabre_token_tile_masks). ``indices`` ``[nb, cap]``
+    ascending, ``counts`` ``[nb]``."""
+    _need_cuda(indices=indices, counts=counts)
+    _i32(indices, "indices")
+    _i32(counts, "counts")
+    L = tok_chunk.numel()
+    csum = torch.cumsum(counts.long(), 0)
+    total = int(csum[-1].item()) if csum.numel() else 0
+    row_ptr = (csum - counts.long()).to(torch.int32).contiguous()
+    masks = torch.empty(max(total, 1), 64, dtype=torch.int64, device=indices.device)
+    st = lib().sabre_token_tile_masks(tok_chunk.data_ptr(), tok_group.data_ptr(), tok_global.data_ptr(),
+                                      dep_bits.data_ptr() if dep_bits.numel() else None, int(nchunks), L, int(window),
+                                      indices.data_ptr(), int(indices.shape[-1]), counts.data_ptr(), row_ptr.data_ptr(),
+                                      masks.data_ptr(), _stream(indices))
+    check(st, "sabre_token_tile_masks")
+    LAUNCHES[0] += 1
+    return masks, row_ptr

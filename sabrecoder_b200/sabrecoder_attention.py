@@ -371,6 +371,15 @@ class StructureAwareMaskBuilder:
             raise NotImplementedError("cross-file prompt chunking (sabrecoder_attention_triton.py:1622-1772) is "
                                       "not part of this library; segment the prompt and call "
                                       "build_block_indices_from_chunks")
+        hit = self._structure_for_code(code, language)
+        return self.build_block_indices_from_chunks(code, seq_len, device, chunks=hit["chunks"],
+                                                    chunk_deps=hit["chunk_deps"], import_chunks=hit["import_chunks"],
+                                                    language=language, batch_size=batch_size)
+
+    def _structure_for_code(self, code: str, language: Optional[str]) -> Dict:
+        """Chunks, dependency edges and import chunks of a prompt from the
+        segmenter and reference analyser (cached per prompt), the gaps filled
+        with line chunks (reference :1774-1797)."""
         key = (hash(code), str(language).lower() if language else None)
         hit = _GLOBAL_CHUNK_CACHE.get(key)
         if hit is None:
@@ -379,15 +388,117 @@ class StructureAwareMaskBuilder:
             imports = {i for i, c in enumerate(chunks) if type_name(c.chunk_type) == "IMPORT"}
             deps: Dict[int, Set[int]] = {}
             for ref in ana(chunks, code, language=language).analyze():
-                s, t = ref.source_chunk_idx, ref.target_chunk_idx
-                deps.setdefault(s, set()).add(t)
-                deps.setdefault(t, set()).add(s)
+                s_, t_ = ref.source_chunk_idx, ref.target_chunk_idx
+                deps.setdefault(s_, set()).add(t_)
+                deps.setdefault(t_, set()).add(s_)
             chunks = self._append_uncovered_line_chunks(code, chunks)
             hit = {"chunks": chunks, "chunk_deps": deps, "import_chunks": imports}
             _cache_put(_GLOBAL_CHUNK_CACHE, key, hit)
-        return self.build_block_indices_from_chunks(code, seq_len, device, chunks=hit["chunks"],
-                                                    chunk_deps=hit["chunk_deps"], import_chunks=hit["import_chunks"],
-                                                    language=language, batch_size=batch_size)
+        return hit
+
+    # ------------------------------------------------------------------
+    # Token-level variant (reference :1171-1454, :1862-1885)
+    # ------------------------------------------------------------------
+    def token_rule_arrays(self, *, code: str, seq_len: int, chunks: Sequence, chunk_deps: Dict[int, Set[int]],
+                          import_chunks: Iterable[int], language: Optional[str]):
+        """Host arrays of the token-level rule: ``(chunk int32[L], group
+        int32[L], global uint8[L], dependency bits uint32[nchunks, words],
+        nchunks)``. Raises like the reference when fewer than 10 % of the
+        tokens map to a chunk (:1256-1264)."""
+        t2c, gtm, flags, ptr, idx = self.structure_to_tokens(code=code, seq_len=seq_len, chunks=chunks,
+                                                             chunk_deps=chunk_deps, import_chunks=import_chunks,
+                                                             language=language)
+        L, n = int(seq_len), len(chunks)
+        valid = t2c >= 0
+        nvalid = int(valid.sum())
+        ratio = nvalid / L if L > 0 else 0.0
+        if ratio < 0.1:
+            raise RuntimeError(f"Token-to-chunk mapping ratio too low ({ratio:.3f}). seq_len={L}, "
+                               f"valid_mappings={nvalid}, num_chunks={n}")
+        glob = gtm.astype(bool)
+        if n > 0:
+            glob |= valid & (flags[np.clip(t2c, 0, n - 1)] & 1).astype(bool)
+            k = int(self.global_last_k_chunks)
+            if k > 0:
+                glob |= valid & (t2c >= max(0, n - k))
+        npre = min(int(self.num_prefix_tokens), L)
+        if npre > 0:
+            glob[:npre] = True
+        nsuf = min(int(self.num_suffix_tokens), L)
+        if nsuf > 0:
+            glob[max(0, L - nsuf):] = True
+        if self.max_chunk_tokens > 0:
+            bpg = max(1, self.max_chunk_tokens // self.block_size)
+            gidx = (np.arange(L) // self.block_size) // bpg
+            ng = int(gidx.max()) + 2 if L > 0 else 2
+            grp = t2c.astype(np.int64) * ng + gidx
+            if n * ng >= 2 ** 31:
+                raise ValueError("too many chunk groups for 32-bit group ids")
+        else:
+            grp = t2c
+        words = max((n + 31) // 32, 1)
+        dep = np.zeros((max(n, 1), words), dtype=np.uint32)
+        for s_ in range(n):
+            for t_ in idx[ptr[s_]:ptr[s_ + 1]]:
+                dep[s_, int(t_) >> 5] |= np.uint32(1 << (int(t_) & 31))
+        return t2c, grp.astype(np.int32), glob.astype(np.uint8), dep, n
+
+    def build_token_level_blocks(self, code: str, seq_len: int, device, *, chunks: Sequence,
+                                 chunk_deps: Dict[int, Set[int]], import_chunks: Iterable[int],
+                                 language: Optional[str] = None, batch_size: int = 1):
+        """Token-level variant without an L x L mask: ``(block_indices [B, nb,
+        max_active], block_counts [B, nb], block_mask_2d [nb, nb], (tile_masks
+        int64 [n_listed, 64], row_ptr int32 [nb]))`` on ``device``. The lists
+        are the blocks holding any visible pair (the reference's block mask of
+        the token mask), ascending; the tile masks hold each listed block's
+        64 query rows' key bits, in list order. Block size 64."""
+        if self.block_size != 64:
+            raise ValueError("the token-level variant uses block_size 64")
+        if self.use_chunk_similarity:
+            sim = self._similarity_edges(chunks, code)
+            if sim:
+                merged = {k: set(v) for k, v in (chunk_deps or {}).items()}
+                for src, tgts in sim.items():
+                    merged.setdefault(src, set()).update(tgts)
+                chunk_deps = merged
+        t2c, grp, glob, dep, n = self.token_rule_arrays(code=code, seq_len=seq_len, chunks=chunks,
+                                                        chunk_deps=chunk_deps, import_chunks=import_chunks,
+                                                        language=language)
+        dev = torch.device(device if device is not None else (self.device or "cuda"))
+
+        def up(a, dt):
+            return torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(dev)
+
+        tc, tg, tgl = up(t2c, torch.int32), up(grp, torch.int32), up(glob, torch.uint8)
+        db = up(dep.view(np.int32), torch.int32)
+        w = int(self.window_size)
+        bits = K.token_block_mask(tc, tg, tgl, db, n, w)
+        nb = bits.shape[0]
+        idx, cnt, mx = K.indices_from_bits(bits, nb)
+        ma = max(int(mx.item()), 1)
+        lists = idx[:, :ma].contiguous()
+        masks, row_ptr = K.token_tile_masks(tc, tg, tgl, db, n, w, lists, cnt)
+        shifts = torch.arange(32, device=dev, dtype=torch.int32)
+        dense = ((bits.unsqueeze(-1) >> shifts) & 1).reshape(nb, -1)[:, :nb].to(torch.int32).contiguous()
+        self.last_block_bits = bits
+        bi = lists.unsqueeze(0).expand(int(batch_size), -1, -1).contiguous()
+        bc = cnt.unsqueeze(0).expand(int(batch_size), -1).contiguous()
+        return bi, bc, dense, (masks, row_ptr)
+
+    def build_token_level_mask(self, code: str, seq_len: int, device, dtype, crossfile_code: Optional[str] = None,
+                               current_code: Optional[str] = None, language: Optional[str] = None,
+                               crossfile_full_attention: bool = True) -> torch.Tensor:
+        """The reference's dense ``(L, L)`` mask, 0 where visible and -inf
+        elsewhere (:1269-1454), expanded from the per-block tile masks. O(L^2)
+        memory: a debugging and compatibility helper; the attention path keeps
+        only the listed blocks' masks."""
+        if crossfile_code is not None and current_code is not None:
+            raise NotImplementedError("cross-file prompt chunking is not part of this library")
+        hit = self._structure_for_code(code, language)
+        bi, bc, _, (masks, row_ptr) = self.build_token_level_blocks(
+            code, seq_len, device, chunks=hit["chunks"], chunk_deps=hit["chunk_deps"],
+            import_chunks=hit["import_chunks"], language=language)
+        return expand_token_masks(bi[0], bc[0], masks, int(seq_len), dtype)
 
     # ------------------------------------------------------------------
     # Chunk-similarity edges (reference :458-682)
@@ -532,6 +643,25 @@ class StructureAwareMaskBuilder:
         clear_all_caches()
 
 
+def expand_token_masks(indices: torch.Tensor, counts: torch.Tensor, tile_masks: torch.Tensor, seq_len: int,
+                       dtype=torch.float32) -> torch.Tensor:
+    """Dense ``(L, L)`` 0/-inf mask from listed blocks' 64-bit row masks."""
+    dev = indices.device
+    nb = indices.shape[0]
+    Lp = nb * 64
+    out = torch.full((nb, 64, nb, 64), float("-inf"), dtype=dtype, device=dev)
+    cnt = counts.long()
+    rows = torch.repeat_interleave(torch.arange(nb, device=dev), cnt)
+    pos = torch.arange(int(cnt.sum().item()), device=dev) - torch.repeat_interleave(torch.cumsum(cnt, 0) - cnt, cnt)
+    cols = indices.long()[rows, pos]
+    shifts = torch.arange(64, device=dev, dtype=torch.int64)
+    bits = ((tile_masks[: rows.numel()].unsqueeze(-1) >> shifts) & 1).bool()  # [n, 64 rows, 64 keys]
+    blk = out[rows, :, cols, :]
+    blk[bits] = 0
+    out[rows, :, cols, :] = blk
+    return out.reshape(Lp, Lp)[:seq_len, :seq_len].contiguous()
+
+
 def deps_to_csr(chunk_deps: Optional[Dict[int, Iterable[int]]], nchunks: int):
     """Dependency dict -> CSR (dep_ptr int32[nchunks+1], dep_idx int32[]),
     dropping out-of-range sources and targets (the reference skips them,
@@ -585,15 +715,16 @@ class StructureAwareSparseAttention(nn.Module):
                  crossfile_chunk_similarity_top_percent: Optional[float] = None, topk_blocks: int = 0,
                  segmenter_factory=None, analyzer_factory=None):
         super().__init__()
-        if use_token_level_sparsity:
-            raise NotImplementedError("the token-level sparse kernel variant is not implemented; "
-                                      "use block-level sparsity")
+        if use_token_level_sparsity and int(block_size) != 64:
+            raise ValueError("use_token_level_sparsity=True needs block_size=64")
+        if use_token_level_sparsity and int(topk_blocks) > 0:
+            raise ValueError("the pooled top-k extension is not combined with token-level sparsity")
         self.tokenizer = tokenizer
         self.block_size = int(block_size)
         self.window_size = window_size
         self.num_prefix_tokens = num_prefix_tokens
         self.num_suffix_tokens = num_suffix_tokens
-        self.use_token_level_sparsity = False
+        self.use_token_level_sparsity = bool(use_token_level_sparsity)
         self.topk_blocks = int(topk_blocks)
         self._bits_cache = None
         self.mask_builder = StructureAwareMaskBuilder(
@@ -624,6 +755,23 @@ class StructureAwareSparseAttention(nn.Module):
             _cache_put(_BLOCK_MASK_CACHE, key, hit)
         return hit
 
+    def _lookup_token_blocks(self, query, code, batch_size):
+        """Token-level lists and tile masks of a prompt (cached). Precomputed
+        block-level lists are not needed here: every visible token pair lies in
+        a block the token rule lists."""
+        mb = self.mask_builder
+        key = ("token", hash(code), query.shape[2], query.device, batch_size, mb.window_size, mb.num_prefix_tokens,
+               mb.num_suffix_tokens, mb.global_last_k_chunks, mb.max_chunk_tokens, mb.use_chunk_similarity)
+        hit = _BLOCK_MASK_CACHE.get(key)
+        if hit is None:
+            st = mb._structure_for_code(code, None)
+            bi, bc, _, tm = mb.build_token_level_blocks(code, query.shape[2], query.device, chunks=st["chunks"],
+                                                        chunk_deps=st["chunk_deps"],
+                                                        import_chunks=st["import_chunks"], batch_size=batch_size)
+            hit = (bi, bc, tm)
+            _cache_put(_BLOCK_MASK_CACHE, key, hit)
+        return hit
+
     def forward(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, code: str = None,
                 attention_mask: Optional[torch.Tensor] = None,
                 precomputed_block_indices: Optional[torch.Tensor] = None,
@@ -631,6 +779,9 @@ class StructureAwareSparseAttention(nn.Module):
                 pooled: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
         B, H, Lq, D = query.shape
         Lk = key.shape[2]
+        if code is not None and Lq == Lk and Lq > 1 and self.use_token_level_sparsity:
+            bi, bc, tm = self._lookup_token_blocks(query, code, B)
+            return K.prefill_bsa(query, key, value, bi, bc, self.block_size, out=out, token_masks=tm)
         if code is not None and Lq == Lk and Lq > 1:
             if precomputed_block_indices is not None and precomputed_block_counts is not None:
                 bi, bc = precomputed_block_indices, precomputed_block_counts

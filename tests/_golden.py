@@ -74,3 +74,14 @@ def sim_case(g, name):
     tgt = g[f"{name}_tgt"].tolist() if sub else None
     edges = deps(g, f"{name}_edge_src", f"{name}_edge_dst")
     return texts, emb, p, src, tgt, edges
+
+
+def token_cases():
+    return sorted(os.path.basename(p) for p in glob.glob(os.path.join(HERE, "token_*.npz")))
+
+
+def token_visible(g):
+    """The reference's token-level visibility restricted to key <= query."""
+    L = int(g["seq_len"])
+    vis = np.unpackbits(g["visible_bits"], axis=-1)[:, :L].astype(bool)
+    return vis & np.tril(np.ones((L, L), dtype=bool))

@@ -22,6 +22,10 @@ What is recorded (all from the reference's own code, unmodified):
 * ``attn_*.npz`` -- ``_fwd_kernel_sabrecoder`` (:28-116) run by Triton's
   interpreter in fp32 on bf16-representable inputs.
 * ``sparsity_utils.json`` -- utils/sparsity_utils.py values.
+* ``token_*.npz`` -- ``_build_mask_from_chunks`` (:1171-1266, the token-level
+  mask of ``use_token_level_sparsity=True``) on seeded chunk sets, stored as
+  packed visibility bits, and ``_fwd_kernel_sabrecoder_token_sparse``
+  (:119-215) run by Triton's interpreter in fp32 with that mask.
 * ``similarity.npz`` -- ``_similarity_edges`` (:581-682, with
   ``_get_or_build_similarity_vectors`` :490-579 and ``_clean_for_similarity``
   :458-472) on seeded chunk texts and a seeded bf16 embedding table, for
@@ -334,6 +338,52 @@ def record_similarity():
     print(f"similarity e2e: nb={nb} density={float(bm.sum()) / (nb * (nb + 1) / 2):.3f}")
 
 
+def record_token_level(name, L, seed, over, tok, language=None, attn_heads=0):
+    """The reference's token-level mask (and, for small cases, its token-level
+    kernel) on a seeded chunk set."""
+    base = dict(window_size=64, num_prefix_tokens=16, num_suffix_tokens=32, block_size=64,
+                global_last_k_chunks=2, max_chunk_tokens=0)
+    params = dict(base, **over)
+    if language == "python":
+        code, chunks = synthetic_python_file(seed)
+        deps = {}
+        imports = {i for i, c in enumerate(chunks) if c.chunk_type == ChunkType.IMPORT}
+    else:
+        ss = make_spans(L, seed, min_len=8, max_len=48, p_function=0.4)
+        code = spans_to_code(ss)
+        chunks = chunks_from_spanset(ss)
+        deps = {int(k): set(int(x) for x in v) for k, v in ss.deps.items()}
+        deps.setdefault(0, set()).add(len(chunks) + 3)  # out of range: skipped
+        imports = set(ss.import_chunks)
+    mb = R.StructureAwareMaskBuilder(tok, **params)
+    mask = mb._build_mask_from_chunks(code, L, torch.device("cpu"), torch.float32, chunks, deps, imports,
+                                      language=language)
+    vis = (mask == 0).numpy()
+    dsrc, ddst = deps_to_arrays(deps)
+    out = dict(code=np.asarray(code), seq_len=L, language=np.asarray(language or ""),
+               tokenizer=np.asarray(tok.name_or_path), **{f"p_{k}": v for k, v in params.items()},
+               **chunk_arrays(chunks), dep_src=dsrc, dep_dst=ddst,
+               import_chunks=np.asarray(sorted(imports), np.int32), visible_bits=np.packbits(vis, axis=-1))
+    if attn_heads:
+        g = torch.Generator().manual_seed(seed + 50)
+        q, k, v = [torch.randn(1, attn_heads, L, 128, generator=g).to(torch.bfloat16).float() for _ in range(3)]
+        bm = R.compute_block_mask_from_token_mask(mask, 64, 64).unsqueeze(0).contiguous()
+        bi, bc = R.compute_block_indices_from_mask(bm)
+        o = torch.empty_like(q)
+        nb = (L + 63) // 64
+        R._fwd_kernel_sabrecoder_token_sparse[(nb, attn_heads)](
+            q, k, v, o, bi, bc, mask, *q.stride(), *k.stride(), *v.stride(), *o.stride(), *bi.stride(),
+            *bc.stride(), *mask.stride(), 1, attn_heads, L, max_active_blocks=bi.shape[2], BLOCK_M=64,
+            BLOCK_N=64, BLOCK_DMODEL=128)
+
+        def bits(x):
+            return x.to(torch.bfloat16).view(torch.int16).numpy()
+
+        out.update(q_bf16=bits(q), k_bf16=bits(k), v_bf16=bits(v), out=o.numpy(), block_mask=bm[0].numpy())
+    np.savez_compressed(os.path.join(HERE, f"token_{name}.npz"), **out)
+    print(f"token_{name}: L={L} visible={vis.mean():.3f} chunks={len(chunks)}")
+
+
 def record_attention(name, B, H, L, D, block, seed):
     g = torch.Generator().manual_seed(seed)
     q, k, v = [torch.randn(B, H, L, D, generator=g).to(torch.bfloat16).float() for _ in range(3)]
@@ -427,6 +477,12 @@ def main():
     record_attention("b128", B=1, H=1, L=300, D=128, block=128, seed=22)
     record_sparsity_utils()
     record_similarity()
+    record_token_level("lines_900", 900, 31, {}, LineTokenizer())
+    record_token_level("groups_1000", 1000, 32, dict(max_chunk_tokens=128, window_size=100, global_last_k_chunks=0),
+                       LineTokenizer())
+    record_token_level("pyspecial_700", 700, 11, dict(num_prefix_tokens=8), WordTokenizer(), language="python")
+    record_token_level("attn_256", 256, 33, dict(window_size=16, global_last_k_chunks=0, num_suffix_tokens=8),
+                       LineTokenizer(), attn_heads=1)
 
 
 if __name__ == "__main__":

@@ -342,3 +342,105 @@ def test_build_block_indices_with_similarity_matches_reference(cuda):
     np.testing.assert_array_equal(bm.cpu().numpy(), g["e2e_block_mask"])
     np.testing.assert_array_equal(bc.cpu().numpy(), g["e2e_block_counts"])
     np.testing.assert_array_equal(bi.cpu().numpy(), g["e2e_indices_sorted"])
+
+
+# ---------------------------------------------------------------------------
+# token-level variant
+# ---------------------------------------------------------------------------
+
+def _token_builder(g):
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder, clear_all_caches
+    clear_all_caches()
+    return StructureAwareMaskBuilder(G.tokenizer(g), **G.params(g))
+
+
+@pytest.mark.parametrize("case", G.token_cases())
+def test_token_level_blocks_match_reference(cuda, case):
+    """Lists = blocks holding a visible pair; the per-block 64x64 masks,
+    expanded, equal the reference's token-level mask (key <= query)."""
+    from sabrecoder_b200.sabrecoder_attention import expand_token_masks
+    g = G.load(case)
+    mb = _token_builder(g)
+    bi, bc, bm, (tm, rp) = mb.build_token_level_blocks(
+        str(g["code"]), int(g["seq_len"]), cuda, chunks=G.chunks(g), chunk_deps=G.deps(g),
+        import_chunks=set(g["import_chunks"].tolist()), language=str(g["language"]) or None)
+    want = G.token_visible(g)
+    wbm = MO.block_mask_from_token_mask(want, 64)
+    np.testing.assert_array_equal(bm.cpu().numpy().astype(bool), wbm)
+    idx, cnt = MO.block_indices_from_mask(wbm)
+    np.testing.assert_array_equal(bc[0].cpu().numpy(), cnt)
+    np.testing.assert_array_equal(bi[0].cpu().numpy()[:, :idx.shape[1]], idx)
+    dense = expand_token_masks(bi[0], bc[0], tm, int(g["seq_len"]))
+    np.testing.assert_array_equal((dense == 0).cpu().numpy(), want)
+
+
+def test_token_level_prefill_matches_reference_kernel(cuda):
+    from sabrecoder_b200 import kernels as K
+    g = G.load("token_attn_256.npz")
+    mb = _token_builder(g)
+    bi, bc, _, tm = mb.build_token_level_blocks(
+        str(g["code"]), int(g["seq_len"]), cuda, chunks=G.chunks(g), chunk_deps=G.deps(g),
+        import_chunks=set(g["import_chunks"].tolist()), language=None)
+    q, k, v = (G.bf16_bits_to_f32(g[n]).to(torch.bfloat16).cuda() for n in ("q_bf16", "k_bf16", "v_bf16"))
+    out = K.prefill_bsa(q, k, v, bi, bc, 64, token_masks=tm)
+    torch.cuda.synchronize()
+    ref = torch.from_numpy(g["out"])
+    err = (out.float().cpu() - ref).abs()
+    assert err.max().item() < 2e-2 and err.mean().item() < 2e-3
+
+
+@pytest.mark.parametrize("case", ["token_lines_900.npz", "token_groups_1000.npz"])
+def test_token_level_prefill_gqa_vs_oracle(cuda, case):
+    from sabrecoder_b200 import kernels as K
+    g = G.load(case)
+    L = int(g["seq_len"])
+    mb = _token_builder(g)
+    bi, bc, _, tm = mb.build_token_level_blocks(
+        str(g["code"]), L, cuda, chunks=G.chunks(g), chunk_deps=G.deps(g),
+        import_chunks=set(g["import_chunks"].tolist()), language=None, batch_size=2)
+    gen = torch.Generator().manual_seed(L)
+    q = torch.randn(2, 4, L, 128, generator=gen).to(torch.bfloat16)
+    k = torch.randn(2, 2, L, 128, generator=gen).to(torch.bfloat16)
+    v = torch.randn(2, 2, L, 128, generator=gen).to(torch.bfloat16)
+    out = K.prefill_bsa(q.cuda(), k.cuda(), v.cuda(), bi, bc, 64, token_masks=tm)
+    torch.cuda.synchronize()
+    ref = AO.token_masked_prefill_fp32(q, k, v, G.token_visible(g))
+    err = (out.float().cpu() - ref).abs()
+    assert err.max().item() < 2e-2 and err.mean().item() < 2e-3
+
+
+def test_attention_module_token_level_end_to_end(cuda):
+    """StructureAwareSparseAttention(use_token_level_sparsity=True) with a
+    fixed segmenter (no analyser edges: the analyser path makes edges
+    symmetric) equals the token-masked oracle."""
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareSparseAttention, clear_all_caches
+    g = G.load("token_attn_256.npz")
+    chunks = G.chunks(g)
+
+    class Seg:
+        def __init__(self, tokenizer=None):
+            pass
+
+        def segment_code(self, code, language=None):
+            return list(chunks)
+
+    class Ana:
+        def __init__(self, chunks, code, language=None):
+            pass
+
+        def analyze(self):
+            return []
+
+    clear_all_caches()
+    mod = StructureAwareSparseAttention(G.tokenizer(g), use_token_level_sparsity=True, segmenter_factory=Seg,
+                                        analyzer_factory=Ana, **G.params(g))
+    q, k, v = (G.bf16_bits_to_f32(g[n]).to(torch.bfloat16) for n in ("q_bf16", "k_bf16", "v_bf16"))
+    out = mod(q.cuda(), k.cuda(), v.cuda(), code=str(g["code"]))
+    torch.cuda.synchronize()
+    imports = {i for i, c in enumerate(chunks) if c.chunk_type.name == "IMPORT"}
+    vis = MO.token_level_mask_from_chunks(code=str(g["code"]), seq_len=int(g["seq_len"]), chunks=chunks,
+                                          chunk_deps={}, import_chunks=imports, language=None,
+                                          tokenizer=G.tokenizer(g), **G.params(g))
+    ref = AO.token_masked_prefill_fp32(q, k, v, vis)
+    err = (out.float().cpu() - ref).abs()
+    assert err.max().item() < 2e-2 and err.mean().item() < 2e-3

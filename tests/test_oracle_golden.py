@@ -178,3 +178,29 @@ def test_similarity_reduction_orders_are_fixed():
     assert abs(n - 1.0) < 2e-3
     sc = MO.similarity_scores(v1[0], v1)
     assert abs(sc[0] - 1.0) < 5e-3 and sc[1] == 0.0
+
+
+@pytest.mark.parametrize("case", G.token_cases())
+def test_token_level_mask_oracle_matches_reference(case):
+    """The oracle's token-level visibility equals the reference's
+    _build_mask_from_chunks (lower triangle; the reference's kernel applies
+    causality), and its block mask lists exactly the blocks with a visible pair."""
+    g = G.load(case)
+    want = G.token_visible(g)
+    got = MO.token_level_mask_from_chunks(
+        code=str(g["code"]), seq_len=int(g["seq_len"]), chunks=G.chunks(g), chunk_deps=G.deps(g),
+        import_chunks=set(g["import_chunks"].tolist()), language=str(g["language"]) or None,
+        tokenizer=G.tokenizer(g), **G.params(g))
+    np.testing.assert_array_equal(got, want)
+    if "block_mask" in g:
+        # recorded from the non-causal _build_mask_from_chunks; the forward path's
+        # mask (build_token_level_mask) is causal, which only drops blocks above
+        # the diagonal (a diagonal block is always listed: distance 0 is in the window)
+        np.testing.assert_array_equal(MO.block_mask_from_token_mask(want, 64), np.tril(g["block_mask"]).astype(bool))
+
+
+def test_token_level_attention_oracle_matches_reference_kernel():
+    g = G.load("token_attn_256.npz")
+    q, k, v = (G.bf16_bits_to_f32(g[n]) for n in ("q_bf16", "k_bf16", "v_bf16"))
+    out = AO.token_masked_prefill_fp32(q, k, v, G.token_visible(g))
+    assert (out - torch.from_numpy(g["out"])).abs().max().item() < 2e-5
