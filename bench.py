@@ -56,6 +56,12 @@ MASK_C4 = dict(block_size=128, window_size=384, num_prefix_tokens=128, num_suffi
                global_last_k_chunks=0)
 
 
+# Fewer definitions than the 1.3B/6.7B mix: with 128-token blocks the sink, the
+# 4-block window and the suffix alone are ~11 % of a 16K causal row, so this
+# mix brings the structure lists to ~14 % (the config asks for ~12 %).
+C4_SPAN_MIX = dict(p_class=0.01, p_function=0.04, header_frac=0.005)
+
+
 def mask_text(mask, topk) -> str:
     return (f"block {mask['block_size']}, window {mask['window_size']}, sink {mask['num_prefix_tokens']}, "
             f"suffix {mask['num_suffix_tokens']}, {mask['max_chunk_tokens']}-token chunk groups"
@@ -132,11 +138,11 @@ def build_model(arch: str, device, rank: int = 0, world: int = 1):
     return model.eval(), cfg
 
 
-def prompt_inputs(L: int, seed: int, vocab: int = 32256):
+def prompt_inputs(L: int, seed: int, vocab: int = 32256, mix=None):
     import numpy as np
     from sabrecoder_b200.spans import BENCH_SPAN_MIX, make_spans
     ids = np.random.default_rng(seed).integers(0, vocab, size=(1, L), dtype=np.int64)
-    spans = make_spans(L, seed, **BENCH_SPAN_MIX)
+    spans = make_spans(L, seed, **(BENCH_SPAN_MIX if mix is None else mix))
     return ids, spans
 
 
@@ -228,6 +234,7 @@ def cpu_layer_sample(arch: str, L: int, seed: int, repeats: int = 1, mask=None, 
     """One decoder layer of the workload on the host cores with the reference's
     dense-masked attention arithmetic; returns (list of seconds per layer call,
     layers, threads). Structure lists and pooled top-k come from the oracle."""
+    mix = C4_SPAN_MIX if mask is MASK_C4 else None
     mask = MASK if mask is None else mask
     topk = TOPK if topk is None else topk
     import numpy as np
@@ -244,7 +251,7 @@ def cpu_layer_sample(arch: str, L: int, seed: int, repeats: int = 1, mask=None, 
     torch.manual_seed(0)
     layer = LlamaDecoderLayer(cfg, 0).float().eval()
     rot = LlamaRotaryEmbedding(cfg)
-    _, spans = prompt_inputs(L, seed)
+    _, spans = prompt_inputs(L, seed, mix=mix)
     base = MO.build_block_mask_tokens(spans.token_to_chunk(), len(spans.spans), spans.import_chunks, spans.deps,
                                       spans.signature_token_mask(), seq_len=L, **mask).astype(bool)
     B = mask["block_size"]
@@ -341,7 +348,7 @@ def run_ours(args, rank, world, dist):
 
     prepared = []
     for L, seed in prompts:
-        ids, spans = prompt_inputs(L, seed, cfg.vocab_size)
+        ids, spans = prompt_inputs(L, seed, cfg.vocab_size, mix=C4_SPAN_MIX if tp else None)
         bi, bc, bm = mb.build_block_indices_from_spans(spans, dev)
         prepared.append((L, torch.from_numpy(ids).to(dev), bi, bc, bm, ids, spans))
     tokens_per_step = sum(p[0] for p in prepared)
