@@ -27,6 +27,7 @@ from __future__ import annotations
 import math
 import re
 from collections import OrderedDict
+from dataclasses import replace
 from typing import Dict, Iterable, List, Optional, Sequence, Set, Tuple
 
 import numpy as np
@@ -70,6 +71,44 @@ def _token_starts(enc, seq_len: int) -> np.ndarray:
         if s is not None and s >= 0:
             st[t] = s
     return st
+
+
+# A retrieved-segment header of a cross-file prompt: "# <path>: <start> - <end>"
+# (Python) or "// <path>: <start> - <end>" (Java), the prompt format the
+# reference's evaluator reads (sabrecoder_attention_triton.py:927-935).
+_SEGMENT_HEADER = re.compile(r"(#|//)\s+.+:\s*\d+\s*-\s*\d+\s*")
+
+
+def crossfile_segments(crossfile_code: str) -> List[Tuple[int, int, str]]:
+    """``(start_line, end_line, text)`` of each retrieved segment of a
+    cross-file context, 1-based inclusive lines (reference :926-985). A
+    segment runs from its header line to the line before the next header; a
+    span of lines before the first header is a segment of its own. Blank-only
+    spans never become segments: they join the segment before them, or the
+    first one after them when none precedes."""
+    lines = crossfile_code.split("\n")
+    heads = [i for i, ln in enumerate(lines, start=1)
+             if ln.rstrip().startswith(("# ", "// ")) and _SEGMENT_HEADER.fullmatch(ln.rstrip())]
+    if heads:
+        spans = ([(1, heads[0] - 1)] if heads[0] > 1 else []) + \
+                [(a, b - 1) for a, b in zip(heads, heads[1:] + [len(lines) + 1])]
+    else:
+        spans = [(1, len(lines))]
+    out: List[List[int]] = []
+    lead: Optional[int] = None  # first line of blank spans seen before any segment
+    for s, e in spans:
+        if e < s:
+            continue
+        if not any(lines[i - 1].strip() for i in range(s, e + 1)):
+            if out:
+                out[-1][1] = max(out[-1][1], e)
+            elif lead is None:
+                lead = s
+            continue
+        if lead is not None:
+            s, lead = min(s, lead), None
+        out.append([s, e])
+    return [(s, e, "\n".join(lines[s - 1 : e])) for s, e in out]
 
 
 def bits_from_indices(block_indices: torch.Tensor, block_counts: torch.Tensor, ncols: int) -> torch.Tensor:
@@ -368,9 +407,13 @@ class StructureAwareMaskBuilder:
         """``(block_indices int32 [B, nb, max_active], block_counts int32 [B, nb],
         block_mask_2d int32 [nb, nb])`` on ``device`` (reference :1606-1819)."""
         if crossfile_code is not None and current_code is not None:
-            raise NotImplementedError("cross-file prompt chunking (sabrecoder_attention_triton.py:1622-1772) is "
-                                      "not part of this library; segment the prompt and call "
-                                      "build_block_indices_from_chunks")
+            hit = self._crossfile_structure(code, crossfile_code, current_code, language, crossfile_full_attention)
+            dense = self._build_block_mask_from_chunks(code=code, seq_len=seq_len, chunks=hit["chunks"],
+                                                       chunk_deps=hit["chunk_deps"],
+                                                       import_chunks=hit["import_chunks"], language=language,
+                                                       device=device)
+            bi, bc = self._indices_from_bits(self.last_block_bits, dense.shape[0], batch_size)
+            return bi, bc, dense
         hit = self._structure_for_code(code, language)
         return self.build_block_indices_from_chunks(code, seq_len, device, chunks=hit["chunks"],
                                                     chunk_deps=hit["chunk_deps"], import_chunks=hit["import_chunks"],
@@ -395,6 +438,65 @@ class StructureAwareMaskBuilder:
             hit = {"chunks": chunks, "chunk_deps": deps, "import_chunks": imports}
             _cache_put(_GLOBAL_CHUNK_CACHE, key, hit)
         return hit
+
+    def _crossfile_structure(self, code: str, crossfile_code: str, current_code: str, language: Optional[str],
+                             full_attention: bool) -> Dict:
+        """Chunks of a cross-file prompt ``code = crossfile_code + current
+        file`` (reference :1622-1772 and :872-1040), similarity edges included:
+
+        * the retrieved context becomes one globally visible chunk
+          (``full_attention``) or one chunk per retrieved segment
+          (:func:`crossfile_segments`);
+        * the current file is segmented and analysed on its own, its gaps
+          filled with line chunks, its lines shifted by the context's line count
+          and its chunk ids by the context's chunk count;
+        * with ``use_chunk_similarity``, current-file chunks link to their most
+          similar context chunks, and with ``use_crossfile_chunk_similarity``
+          context chunks link among themselves at
+          ``crossfile_chunk_similarity_top_percent``."""
+        if not code.startswith(crossfile_code):
+            raise ValueError("full_code does not start with crossfile_code; dataset fields are inconsistent.")
+        shift = len(crossfile_code.split("\n")) if crossfile_code else 0
+        chunks: List = []
+        global_chunks: Set[int] = set()
+        if crossfile_code and crossfile_code.strip():
+            if full_attention:
+                chunks.append(CodeChunk(ChunkType.MODULE_CODE, 0, len(crossfile_code), crossfile_code, "", None,
+                                        1, shift, None, None))
+                global_chunks.add(0)
+            else:
+                for s, e, text in crossfile_segments(crossfile_code):
+                    chunks.append(CodeChunk(ChunkType.MODULE_CODE, 0, len(text), text, "", None, s, e, None, None))
+        ncf = len(chunks)
+        deps: Dict[int, Set[int]] = {}
+        imports: Set[int] = set()
+        if current_code and current_code.strip():
+            seg, ana = self._structure_backends()
+            cur = seg(tokenizer=self.tokenizer).segment_code(current_code, language=language)
+            for c in self._append_uncovered_line_chunks(current_code, cur):
+                chunks.append(replace(
+                    c, start_line=c.start_line + shift, end_line=c.end_line + shift,
+                    signature_start_line=(c.signature_start_line + shift) if c.signature_start_line else None,
+                    signature_end_line=(c.signature_end_line + shift) if c.signature_end_line else None))
+            # Analyser ids index the segmenter's own list, which the gap
+            # chunks extend at the end, so shifting by ncf keeps them valid.
+            for ref in ana(cur, current_code, language=language).analyze():
+                s_, t_ = ref.source_chunk_idx + ncf, ref.target_chunk_idx + ncf
+                deps.setdefault(s_, set()).add(t_)
+                deps.setdefault(t_, set()).add(s_)
+            imports = {i + ncf for i, c in enumerate(cur) if type_name(c.chunk_type) == "IMPORT"}
+        if self.use_chunk_similarity:
+            sim = self._similarity_edges(chunks, code, src_indices=list(range(ncf, len(chunks))),
+                                         tgt_indices=list(range(ncf)))
+            for s_, tg in sim.items():
+                deps.setdefault(s_, set()).update(tg)
+            if self.use_crossfile_chunk_similarity and ncf > 1:
+                cf = list(range(ncf))
+                sim = self._similarity_edges(chunks, code, src_indices=cf, tgt_indices=cf,
+                                             top_percent=self.crossfile_chunk_similarity_top_percent)
+                for s_, tg in sim.items():
+                    deps.setdefault(s_, set()).update(tg)
+        return {"chunks": chunks, "chunk_deps": deps, "import_chunks": imports | global_chunks}
 
     # ------------------------------------------------------------------
     # Token-level variant (reference :1171-1454, :1862-1885)
@@ -445,16 +547,19 @@ class StructureAwareMaskBuilder:
 
     def build_token_level_blocks(self, code: str, seq_len: int, device, *, chunks: Sequence,
                                  chunk_deps: Dict[int, Set[int]], import_chunks: Iterable[int],
-                                 language: Optional[str] = None, batch_size: int = 1):
+                                 language: Optional[str] = None, batch_size: int = 1,
+                                 merge_similarity: bool = True):
         """Token-level variant without an L x L mask: ``(block_indices [B, nb,
         max_active], block_counts [B, nb], block_mask_2d [nb, nb], (tile_masks
         int64 [n_listed, 64], row_ptr int32 [nb]))`` on ``device``. The lists
         are the blocks holding any visible pair (the reference's block mask of
         the token mask), ascending; the tile masks hold each listed block's
-        64 query rows' key bits, in list order. Block size 64."""
+        64 query rows' key bits, in list order. Block size 64.
+        ``merge_similarity=False`` takes ``chunk_deps`` as final (the
+        cross-file path has merged its own similarity edges)."""
         if self.block_size != 64:
             raise ValueError("the token-level variant uses block_size 64")
-        if self.use_chunk_similarity:
+        if self.use_chunk_similarity and merge_similarity:
             sim = self._similarity_edges(chunks, code)
             if sim:
                 merged = {k: set(v) for k, v in (chunk_deps or {}).items()}
@@ -493,11 +598,13 @@ class StructureAwareMaskBuilder:
         memory: a debugging and compatibility helper; the attention path keeps
         only the listed blocks' masks."""
         if crossfile_code is not None and current_code is not None:
-            raise NotImplementedError("cross-file prompt chunking is not part of this library")
-        hit = self._structure_for_code(code, language)
+            hit = self._crossfile_structure(code, crossfile_code, current_code, language, crossfile_full_attention)
+        else:
+            hit = self._structure_for_code(code, language)
         bi, bc, _, (masks, row_ptr) = self.build_token_level_blocks(
             code, seq_len, device, chunks=hit["chunks"], chunk_deps=hit["chunk_deps"],
-            import_chunks=hit["import_chunks"], language=language)
+            import_chunks=hit["import_chunks"], language=language,
+            merge_similarity=crossfile_code is None or current_code is None)
         return expand_token_masks(bi[0], bc[0], masks, int(seq_len), dtype)
 
     # ------------------------------------------------------------------

@@ -85,3 +85,48 @@ def token_visible(g):
     L = int(g["seq_len"])
     vis = np.unpackbits(g["visible_bits"], axis=-1)[:, :L].astype(bool)
     return vis & np.tril(np.ones((L, L), dtype=bool))
+
+
+def crossfile_case(g, name):
+    """Fields of one crossfile.npz case, without the case prefix; the
+    segmenter's chunks come back as this library's CodeChunk objects."""
+    from sabrecoder_b200.chunks import ChunkType, CodeChunk
+    c = {k[len(name) + 1:]: v for k, v in g.items() if k.startswith(name + "_")}
+    seg = []
+    for i, ch in enumerate(chunks(c, "seg_")):
+        seg.append(CodeChunk(ChunkType[ch.chunk_type.name], 0, 0, str(c["seg_texts"][i]), name=ch.name,
+                             start_line=ch.start_line, end_line=ch.end_line,
+                             signature_start_line=ch.signature_start_line,
+                             signature_end_line=ch.signature_end_line))
+    c["seg_chunks"] = seg
+    c["ref_chunks"] = chunks(c, "ref_")
+    c["ref_deps"] = deps(c, "ref_dep_src", "ref_dep_dst")
+    return c
+
+
+def crossfile_builder(c, **extra):
+    """A StructureAwareMaskBuilder with the case's parameters and a fixed
+    segmenter / analyser standing in for tree-sitter."""
+    import torch
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+    from sabrecoder_b200.spans import HashTokenizer
+
+    class Seg:
+        def __init__(self, tokenizer=None):
+            pass
+
+        def segment_code(self, code, language=None):
+            return list(c["seg_chunks"])
+
+    class Ana:
+        def __init__(self, chunks_, code, language=None):
+            pass
+
+        def analyze(self):
+            return [SimpleNamespace(source_chunk_idx=int(a), target_chunk_idx=int(b))
+                    for a, b in zip(c["edge_src"].tolist(), c["edge_dst"].tolist())]
+
+    p = {k[2:]: c[k].item() for k in c if k.startswith("p_")}
+    emb = bf16_bits_to_f32(c["emb_bf16"]).to(torch.bfloat16)
+    return StructureAwareMaskBuilder(HashTokenizer(128), embedding_weight=emb, segmenter_factory=Seg,
+                                     analyzer_factory=Ana, **p, **extra)

@@ -428,6 +428,126 @@ def record_sparsity_utils():
     print("sparsity_utils.json")
 
 
+def crossfile_prompt(seed, n_segs, java=False, lead=()):
+    """A seeded cross-file prompt in the evaluator's format: retrieved segments
+    as commented lines under "<mark> <path>: <start> - <end>" headers (plus
+    look-alike lines that are not headers and blank lines), then the current
+    file as chunk texts; returns (crossfile, current, current chunk list)."""
+    rng = np.random.default_rng(seed)
+    mark = "// " if java else "# "
+    shared = [f"w{i}" for i in range(40)]
+    cf = list(lead)
+    for s in range(n_segs):
+        a = int(rng.integers(1, 200))
+        cf.append(f"{mark}pkg/m{s}.{'java' if java else 'py'}: {a} - {a + int(rng.integers(3, 30))}" +
+                  ("   " if s % 3 == 1 else ""))
+        for _ in range(int(rng.integers(2, 9))):
+            words = [shared[int(rng.integers(0, len(shared)))] for _ in range(int(rng.integers(1, 6)))]
+            cf.append(mark + " ".join(words) + f" s{s}")
+        if s % 4 == 2:
+            cf.append(f"{mark}note: 3 - x")      # trailing text: not a header
+            cf.append(mark.strip() + f"pkg/z.py: 1 - 2")  # no space after the mark: not a header
+        if s % 2 == 0:
+            cf.append("")
+    crossfile = "\n".join(cf) + "\n\n"
+    texts = similarity_texts(seed + 1, n_chunks=30)
+    lines, chunks = [], []
+    for i, t in enumerate(texts):
+        s0 = len(lines) + 1
+        lines.extend(t.split("\n"))
+        kind = ChunkType.IMPORT if i < 2 else (ChunkType.FUNCTION if i % 4 == 0 else ChunkType.MODULE_CODE)
+        if i % 6 == 5:
+            continue  # left for the gap filler
+        sig = s0 if kind == ChunkType.FUNCTION else None
+        chunks.append(CodeChunk(kind, 0, 0, t, name=f"c{i}", start_line=s0, end_line=len(lines),
+                                signature_start_line=sig, signature_end_line=sig))
+    return crossfile, "\n".join(lines), chunks
+
+
+def record_crossfile():
+    """build_block_indices and build_token_level_mask with crossfile_code /
+    current_code (reference :1622-1772, :860-1081): the chunks, edges and
+    imports the reference assembles (captured from its
+    _build_block_mask_from_chunks call) and its block and token masks."""
+    tok = HashTokenizer(vocab=128)
+    out = {}
+    cases = [
+        # name, seed, segments, java, lead lines, full attention, similarity, crossfile similarity, block
+        ("full", 40, 6, False, (), True, True, True, 16),
+        ("seg", 41, 9, False, ("", "  "), False, True, True, 16),
+        ("segjava", 42, 7, True, ("// leading w1 w2", ""), False, False, False, 32),
+        ("segtok", 43, 5, False, (), False, True, False, 64),
+    ]
+    for name, seed, nseg, java, lead, full, sim, cfsim, block in cases:
+        crossfile, current, seg_chunks = crossfile_prompt(seed, nseg, java, lead)
+        code = crossfile + current
+        L = len(tok(code)["input_ids"])
+        fun = [i for i, c in enumerate(seg_chunks) if c.chunk_type == ChunkType.FUNCTION]
+        edges = [(a, b) for a, b in zip(fun[1::2], fun[::2])]
+
+        class Seg:
+            def __init__(self, tokenizer=None):
+                pass
+
+            def segment_code(self, code, language=None):
+                return list(seg_chunks)
+
+        class Ana:
+            def __init__(self, chunks, code, language=None):
+                pass
+
+            def analyze(self):
+                return [_Ref(a, b) for a, b in edges]
+
+        R.TreeSitterSegmenter, R.CrossReferenceAnalyzer = Seg, Ana
+        g = torch.Generator().manual_seed(seed + 500)
+        emb = torch.randn(128, 128, generator=g).to(torch.bfloat16)
+        params = dict(window_size=32, num_prefix_tokens=8, num_suffix_tokens=24, block_size=block,
+                      global_last_k_chunks=1, max_chunk_tokens=0)
+        simp = dict(use_chunk_similarity=sim, embedding_weight=emb, chunk_similarity_top_percent=0.2,
+                    chunk_similarity_max_neighbors=3, chunk_similarity_max_tokens_per_chunk=64,
+                    use_crossfile_chunk_similarity=cfsim, crossfile_chunk_similarity_top_percent=0.3)
+        mb = R.StructureAwareMaskBuilder(tok, **params, **simp)
+        seen = {}
+        inner = mb._build_block_mask_from_chunks
+
+        def spy(**kw):
+            seen.update(kw)
+            return inner(**kw)
+
+        mb._build_block_mask_from_chunks = spy
+        bi, bc, bm = mb.build_block_indices(code, L, torch.device("cpu"), crossfile_code=crossfile,
+                                            current_code=current, crossfile_full_attention=full)
+        nb = bm.shape[0]
+        canon = np.full(bi.shape, -1, np.int32)
+        for r in range(nb):
+            c = int(bc[0, r])
+            canon[0, r, :c] = np.sort(bi[0, r, :c].numpy())
+        esrc, edst = deps_to_arrays(seen["chunk_deps"])
+        rec = {"code": np.asarray(code), "crossfile": np.asarray(crossfile), "current": np.asarray(current),
+               "seq_len": L, "full_attention": np.asarray(full), "emb_bf16": emb.view(torch.int16).numpy(),
+               **{f"p_{k}": np.asarray(v) for k, v in params.items()},
+               **{f"p_{k}": np.asarray(v) for k, v in simp.items() if k != "embedding_weight"},
+               **{f"seg_{k}": v for k, v in chunk_arrays(seg_chunks).items()},
+               "seg_texts": np.asarray([c.text for c in seg_chunks]),
+               "edge_src": np.asarray([a for a, _ in edges], np.int32),
+               "edge_dst": np.asarray([b for _, b in edges], np.int32),
+               **{f"ref_{k}": v for k, v in chunk_arrays(seen["chunks"]).items()},
+               "ref_texts": np.asarray([c.text for c in seen["chunks"]]),
+               "ref_dep_src": esrc, "ref_dep_dst": edst,
+               "ref_imports": np.asarray(sorted(seen["import_chunks"]), np.int32),
+               "block_mask": bm.numpy().astype(np.uint8), "block_counts": bc.numpy(), "indices_sorted": canon}
+        if block == 64:
+            mask = mb.build_token_level_mask(code, L, torch.device("cpu"), torch.float32, crossfile_code=crossfile,
+                                             current_code=current, crossfile_full_attention=full)
+            rec["visible_bits"] = np.packbits((mask == 0).numpy(), axis=-1)
+        out.update({f"{name}_{k}": v for k, v in rec.items()})
+        print(f"crossfile {name}: L={L} nb={nb} chunks={len(seen['chunks'])} edges={len(esrc)} "
+              f"density={float(bm.sum()) / (nb * (nb + 1) / 2):.3f}")
+    out["cases"] = np.asarray([c[0] for c in cases])
+    np.savez_compressed(os.path.join(HERE, "crossfile.npz"), **out)
+
+
 def main():
     base = dict(window_size=192, num_prefix_tokens=64, num_suffix_tokens=128, block_size=64,
                 global_last_k_chunks=0, max_chunk_tokens=128)
@@ -483,7 +603,14 @@ def main():
     record_token_level("pyspecial_700", 700, 11, dict(num_prefix_tokens=8), WordTokenizer(), language="python")
     record_token_level("attn_256", 256, 33, dict(window_size=16, global_last_k_chunks=0, num_suffix_tokens=8),
                        LineTokenizer(), attn_heads=1)
+    record_crossfile()
 
 
 if __name__ == "__main__":
-    main()
+    # No argument: every fixture. Otherwise the named recorders only, e.g.
+    # "python tests/golden/gen_golden.py crossfile".
+    if len(sys.argv) > 1:
+        for _n in sys.argv[1:]:
+            globals()[f"record_{_n}"]()
+    else:
+        main()
