@@ -121,6 +121,32 @@ def test_prefill_empty_lists_give_zero_rows(K):
     assert out[:, :, 128:256].abs().max().item() == 0.0
 
 
+@pytest.mark.parametrize("block", [64, 128])
+def test_prefill_many_items_ragged(K, block):
+    """Several 128-row tiles per CTA (more tiles than SMs) with ragged lists:
+    empty tiles, tiles with one key block, odd and even counts, per head; the
+    tiles of one CTA run back to back, so each must start its accumulators
+    and running statistics afresh."""
+    gen = torch.Generator().manual_seed(17 + block)
+    B, H, L, D = 2, 12, 3000, 128
+    q, k, v = (torch.randn(B, H, L, D, generator=gen).to(torch.bfloat16) for _ in range(3))
+    nb = (L + block - 1) // block
+    m = torch.rand(B, H, nb, nb, generator=gen) < 0.15
+    kind = torch.randint(0, 5, (B, H, nb), generator=gen)
+    m[kind == 0] = False                                   # empty row
+    one = torch.zeros(B, H, nb, nb, dtype=torch.bool)
+    one[..., 0] = True
+    m = torch.where((kind == 1).unsqueeze(-1), one, m)     # only the first block
+    m = m | (torch.eye(nb, dtype=torch.bool) & (kind != 0).unsqueeze(-1))
+    idx, cnt = MO.block_indices_from_mask(m.tril().numpy())
+    bi, bc = torch.from_numpy(idx), torch.from_numpy(cnt)
+    out = K.prefill_bsa(q.cuda(), k.cuda(), v.cuda(), bi.cuda(), bc.cuda(), block)
+    torch.cuda.synchronize()
+    ref = AO.sparse_prefill_fp32(q, k, v, bi, bc, block)
+    _close(out, ref)
+    assert K.device_status() == 0
+
+
 def test_prefill_config0_shape(K):
     """B=1, H=16, L=4096, D=128, block 64 with a structure mask + top-8."""
     gen = torch.Generator().manual_seed(0)
