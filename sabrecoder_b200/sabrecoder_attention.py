@@ -20,6 +20,9 @@ Tree-sitter segmentation and the reference graph (semantic_chunker.py,
 reference_graph.py) are pluggable: pass ``segmenter_factory`` /
 ``analyzer_factory`` (same interfaces as the reference classes) or call the
 ``*_from_chunks`` / ``*_from_spans`` entry points with ready-made structure.
+Without them, the reference's tree-sitter modules are used when importable,
+else the built-in Python segmenter and analyser of
+:mod:`sabrecoder_b200.structure`.
 """
 
 from __future__ import annotations
@@ -734,14 +737,18 @@ class StructureAwareMaskBuilder:
         return edges
 
     def _structure_backends(self):
+        """Segmenter and analyser classes: the ones passed to the constructor,
+        else the reference's tree-sitter modules when importable, else the
+        built-in Python ones (:mod:`sabrecoder_b200.structure`, Python source
+        only; other languages raise there)."""
         seg, ana = self.segmenter_factory, self.analyzer_factory
         if seg is None or ana is None:
             try:
                 from semantic_chunker import TreeSitterSegmenter  # the reference's segmenter, if importable
                 from reference_graph import CrossReferenceAnalyzer
-            except Exception as e:  # noqa: BLE001
-                raise RuntimeError("code segmentation needs tree-sitter (semantic_chunker / reference_graph); pass "
-                                   "segmenter_factory/analyzer_factory or use build_block_indices_from_chunks") from e
+            except Exception:  # noqa: BLE001  (tree-sitter not installed)
+                from .structure import PythonReferenceAnalyzer as CrossReferenceAnalyzer
+                from .structure import PythonSegmenter as TreeSitterSegmenter
             seg = seg or TreeSitterSegmenter
             ana = ana or CrossReferenceAnalyzer
         return seg, ana

@@ -548,6 +548,218 @@ def record_crossfile():
     np.savez_compressed(os.path.join(HERE, "crossfile.npz"), **out)
 
 
+# --------------------------------------------------------------------------
+# Structure analysis (segmenter + cross-reference analyser) for Python.
+# tree-sitter is not installed here, so the reference's TreeSitterSegmenter and
+# CrossReferenceAnalyzer are driven through a stand-in parser that presents the
+# standard ast module's tree with tree-sitter-python's node types and fields
+# (function_definition, class_definition, import_statement,
+# import_from_statement, call/function, attribute, identifier, ...). The
+# fixtures therefore pin the reference's rules (walk, chunk kinds, names, gap
+# filling, callee matching) on ast's parse of the source; tree-sitter's own
+# parse is the part they cannot pin.
+# --------------------------------------------------------------------------
+import ast as _ast  # noqa: E402
+import re as _re  # noqa: E402
+
+
+class _TSNode:
+    def __init__(self, kind, a, b, pa, pb, children=(), fields=None):
+        self.type = kind
+        self.start_byte, self.end_byte = a, b
+        self.start_point, self.end_point = pa, pb
+        self.children = list(children)
+        self.named_children = self.children
+        self._fields = fields or {}
+
+    def child_by_field_name(self, name):
+        return self._fields.get(name)
+
+
+class _TSTree:
+    def __init__(self, root):
+        self.root_node = root
+
+
+class _AstAsTreeSitter:
+    """parse(bytes) -> a tree-sitter-shaped tree built from ast."""
+
+    def parse(self, data):
+        code = data.decode("utf-8")
+        self.data = data
+        self.starts = [0] + [m.end() for m in _re.finditer(b"\n", data)]
+        mod = _ast.parse(code)
+        kids = [self.conv(n) for n in mod.body]
+        end = len(data)
+        return _TSTree(_TSNode("module", 0, end, (0, 0), self.point(end), kids))
+
+    def point(self, byte):
+        row = max(i for i, st in enumerate(self.starts) if st <= byte)
+        return (row, byte - self.starts[row])
+
+    def pos(self, node):
+        a = self.starts[node.lineno - 1] + node.col_offset
+        b = self.starts[node.end_lineno - 1] + node.end_col_offset
+        return a, b
+
+    def mk(self, kind, a, b, children=(), fields=None):
+        return _TSNode(kind, a, b, self.point(a), self.point(b), children, fields)
+
+    def ident_after(self, a, name, kw):
+        i = self.data.find(kw, a) + len(kw)
+        i = self.data.find(name.encode(), i)
+        return self.mk("identifier", i, i + len(name.encode()))
+
+    def span(self, kind, kids):
+        kids = [k for k in kids if k is not None]
+        if not kids:
+            return None
+        return self.mk(kind, min(k.start_byte for k in kids), max(k.end_byte for k in kids), kids)
+
+    def conv(self, n):
+        if n is None:
+            return None
+        if isinstance(n, (_ast.FunctionDef, _ast.AsyncFunctionDef, _ast.ClassDef)):
+            a, b = self.pos(n)
+            is_cls = isinstance(n, _ast.ClassDef)
+            name = self.ident_after(a, n.name, b"class" if is_cls else b"def")
+            if is_cls:
+                args = self.span("argument_list", [self.conv(x) for x in n.bases + n.keywords])
+                kids = [name, args, self.span("block", [self.conv(x) for x in n.body])]
+                node = self.mk("class_definition", a, b, [k for k in kids if k is not None])
+            else:
+                ar = n.args
+                params = [self.conv(x) for x in ar.posonlyargs + ar.args + ([ar.vararg] if ar.vararg else [])
+                          + ar.kwonlyargs + ([ar.kwarg] if ar.kwarg else [])]
+                params += [self.conv(x) for x in ar.defaults + [d for d in ar.kw_defaults if d is not None]]
+                kids = [name, self.span("parameters", params), self.conv(n.returns),
+                        self.span("block", [self.conv(x) for x in n.body])]
+                node = self.mk("function_definition", a, b, [k for k in kids if k is not None])
+            if n.decorator_list:
+                decs = [self.mk("decorator", *self.pos(d), [self.conv(d)]) for d in n.decorator_list]
+                return self.mk("decorated_definition", decs[0].start_byte, b, decs + [node])
+            return node
+        if isinstance(n, _ast.Import):
+            return self.mk("import_statement", *self.pos(n))
+        if isinstance(n, _ast.ImportFrom):
+            return self.mk("import_from_statement", *self.pos(n))
+        if isinstance(n, _ast.Call):
+            fn = self.conv(n.func)
+            args = self.span("argument_list", [self.conv(x) for x in n.args + n.keywords])
+            a, b = self.pos(n)
+            return self.mk("call", a, b, [k for k in (fn, args) if k is not None],
+                           {"function": fn, "arguments": args})
+        if isinstance(n, _ast.Name):
+            return self.mk("identifier", *self.pos(n))
+        if isinstance(n, _ast.arg):
+            a = self.starts[n.lineno - 1] + n.col_offset
+            ident = self.mk("identifier", a, a + len(n.arg.encode()))
+            ann = self.conv(n.annotation)
+            return ident if ann is None else self.span("typed_parameter", [ident, ann])
+        if isinstance(n, _ast.Attribute):
+            a, b = self.pos(n)
+            attr = self.mk("identifier", b - len(n.attr.encode()), b)
+            return self.mk("attribute", a, b, [self.conv(n.value), attr])
+        if isinstance(n, _ast.keyword):
+            val = self.conv(n.value)
+            if n.arg is None:
+                return self.span("dictionary_splat", [val])
+            a = self.starts[n.lineno - 1] + n.col_offset
+            return self.span("keyword_argument", [self.mk("identifier", a, a + len(n.arg.encode())), val])
+        if isinstance(n, _ast.Lambda):
+            a, b = self.pos(n)
+            ar = n.args
+            params = [self.conv(x) for x in ar.posonlyargs + ar.args + ar.kwonlyargs]
+            kids = [self.span("lambda_parameters", params), self.conv(n.body)]
+            return self.mk("lambda", a, b, [k for k in kids if k is not None])
+        kids = [self.conv(c) for c in _ast.iter_child_nodes(n)]
+        kids = [k for k in kids if k is not None]
+        if hasattr(n, "lineno") and getattr(n, "end_lineno", None) is not None:
+            return self.mk("x_" + type(n).__name__.lower(), *self.pos(n), kids)
+        return self.span("x_" + type(n).__name__.lower(), kids)
+
+
+def structure_python_file(seed, n_units=30):
+    """A seeded Python file with the constructs the structure rules care
+    about: imports at the top and nested in if/try/classes, decorated and async
+    functions, nested classes and functions, methods calling each other,
+    attribute / chained / keyword / lambda calls, comments and blank runs."""
+    rng = np.random.default_rng(seed)
+    names = [f"f{u}" for u in range(n_units)]
+    L = ["", "# header comment", "", "import os", "import sys as _sys", "from typing import (", "    List,",
+         "    Dict,", ")", "try:", "    import json", "except ImportError:", "    json = None", "",
+         "if _sys.version_info >= (3, 8):", "    from functools import cache", "else:",
+         "    def cache(f):", "        return f", ""]
+    for u in range(n_units):
+        r = rng.random()
+        callee = names[int(rng.integers(0, n_units))]
+        other = names[int(rng.integers(0, n_units))]
+        if r < 0.25:
+            L += ([f"@cache"] if u % 2 else []) + [f"def {names[u]}(a, b=len('x'), *args, k=None, **kw):",
+                                                   f"    \"\"\"Doc {u}.\"\"\"",
+                                                   f"    x = {callee}(a, b) + obj.{other}(k=k)",
+                                                   f"    return (lambda q: {callee}(q))(x)", ""]
+        elif r < 0.45:
+            L += [f"class C{u}(Base{u % 3}, metaclass=Meta):", f"    attr = {callee}(1)",
+                  "    import re", f"    def {names[u]}(self):", f"        return self.{other}()",
+                  "", f"    @property", f"    def p{u}(self):", f"        return {callee}(self)[0]",
+                  f"    class Inner{u}:", f"        def {other}(self, x):",
+                  f"            return C{u}.{names[u]}(x).{callee}()", ""]
+        elif r < 0.6:
+            L += [f"async def {names[u]}(x):", f"    await {callee}(x)", f"    def inner_{u}():",
+                  f"        return {other}()", f"    return inner_{u}()", ""]
+        elif r < 0.8:
+            L += [f"RESULT_{u} = {callee}({other}(1), key=lambda v: v)", "", "", f"# comment {u}"]
+        else:
+            L += [f"for i in range({u}):", f"    {callee}(i)", "", "with open('f') as fh:",
+                  f"    def {names[u]}(z):", f"        return {other}(z)", ""]
+    L += ["", "if __name__ == '__main__':", f"    {names[0]}(1, 2)", "", ""]
+    return "\n".join(L)
+
+
+def record_structure():
+    """TreeSitterSegmenter.segment_code and CrossReferenceAnalyzer.analyze on
+    seeded Python files, through the ast-backed stand-in parser."""
+    import reference_graph as RG
+    import semantic_chunker as SC
+    SC.get_parser = lambda lang: _AstAsTreeSitter()
+    RG.get_parser = lambda lang: _AstAsTreeSitter()
+    out = {}
+    files = [("s0", structure_python_file(60)), ("s1", structure_python_file(61, 45)),
+             ("s2", synthetic_python_file(62)[0]), ("s3", "\n\n\ndef only():\n    return only()\n\n\n")]
+    for name, code in files:
+        chunks = SC.TreeSitterSegmenter().segment_code(code, language="python")
+        refs = RG.CrossReferenceAnalyzer(chunks, code, language="python").analyze()
+        rows = sorted((r.source_chunk_idx, r.target_chunk_idx, r.line_number, r.name) for r in refs)
+        out.update({f"{name}_code": np.asarray(code), **{f"{name}_{k}": v for k, v in chunk_arrays(chunks).items()},
+                    f"{name}_start": np.asarray([c.start for c in chunks], np.int64),
+                    f"{name}_end": np.asarray([c.end for c in chunks], np.int64),
+                    f"{name}_parent": np.asarray([c.parent_name or "" for c in chunks]),
+                    f"{name}_text": np.asarray([c.text for c in chunks]),
+                    f"{name}_ref_src": np.asarray([r[0] for r in rows], np.int32),
+                    f"{name}_ref_dst": np.asarray([r[1] for r in rows], np.int32),
+                    f"{name}_ref_line": np.asarray([r[2] for r in rows], np.int32),
+                    f"{name}_ref_name": np.asarray([r[3] for r in rows])})
+        if name in ("s0", "s1"):
+            # build_block_indices on the raw source, the structure coming from
+            # the segmenter and analyser above (language "python": special
+            # lines are on).
+            tok = HashTokenizer(vocab=128)
+            L = len(tok(code)["input_ids"])
+            params = dict(window_size=32, num_prefix_tokens=8, num_suffix_tokens=24, block_size=16,
+                          global_last_k_chunks=1, max_chunk_tokens=64)
+            R.TreeSitterSegmenter, R.CrossReferenceAnalyzer = SC.TreeSitterSegmenter, RG.CrossReferenceAnalyzer
+            R._GLOBAL_CHUNK_CACHE.clear()
+            mb = R.StructureAwareMaskBuilder(tok, **params)
+            _, bc, bm = mb.build_block_indices(code, L, torch.device("cpu"), language="python")
+            out.update({f"{name}_seq_len": np.asarray(L), f"{name}_block_mask": bm.numpy().astype(np.uint8),
+                        f"{name}_block_counts": bc.numpy(),
+                        **{f"{name}_p_{k}": np.asarray(v) for k, v in params.items()}})
+        print(f"structure {name}: lines {code.count(chr(10)) + 1} chunks {len(chunks)} refs {len(rows)}")
+    out["files"] = np.asarray([f for f, _ in files])
+    np.savez_compressed(os.path.join(HERE, "structure.npz"), **out)
+
+
 def main():
     base = dict(window_size=192, num_prefix_tokens=64, num_suffix_tokens=128, block_size=64,
                 global_last_k_chunks=0, max_chunk_tokens=128)
@@ -604,6 +816,7 @@ def main():
     record_token_level("attn_256", 256, 33, dict(window_size=16, global_last_k_chunks=0, num_suffix_tokens=8),
                        LineTokenizer(), attn_heads=1)
     record_crossfile()
+    record_structure()
 
 
 if __name__ == "__main__":
