@@ -439,6 +439,7 @@ def run_ours(args, rank, world, dist):
                "sample": f"1 of {layers} decoder layers (fp32, dense-masked SDPA per head) on {L0} tokens, "
                          f"scaled x{layers}; embeddings/lm_head excluded"}
 
+    weight_gb = sum(p.numel() * p.element_size() for p in model.parameters()) / 1e9
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -448,9 +449,10 @@ def run_ours(args, rank, world, dist):
                                    f"{'+'.join(str(p[0]) for p in prepared)} tokens "
                                    f"{'per job' if tp else 'per GPU'}, {mask_text(mask, topk)}",
                        "seq_len": prepared[0][0], "global_batch": len(prompts) * (world if scaling == "weak" else 1),
-                       "parallelism": (f"head-parallel TP x{world}: NCCL all-reduce after o_proj and down_proj"
+                       "parallelism": (f"head-parallel TP x{world} with sequence parallelism: NCCL reduce-scatter "
+                                       f"after o_proj and down_proj, all-gather before attention and MLP"
                                        if tp and world > 1 else f"prompt-parallel x{world}, no collectives"),
-                       "l2": "inputs larger than L2 (2.6 GB of weights read per step)",
+                       "l2": f"inputs larger than L2 ({weight_gb:.1f} GB of weights read per step per GPU)",
                        "density_structure": round(statistics.mean(dens), 4),
                        "density_with_topk": round(act / tot_blocks, 4) if tot_blocks else None},
             "attn_tflops": kf / (kt * 1e-3) / 1e12 if kt > 0 else None,

@@ -109,10 +109,10 @@ def _tiny_model():
     return LlamaForCausalLM(_tiny_cfg()).float().eval()
 
 
-def _tiny_inputs():
+def _tiny_inputs(L=320):
     from oracle import mask_oracle as MO
     from sabrecoder_b200.spans import make_spans
-    L, blk = 320, 64
+    blk = 64
     sp = make_spans(L, 11)
     m = MO.build_block_mask_tokens(sp.token_to_chunk(), len(sp.spans), sp.import_chunks, sp.deps,
                                    sp.signature_token_mask(), seq_len=L, block_size=blk, window_size=64,
@@ -130,26 +130,34 @@ def _logits(model, ids, bi, bc, blk):
         return model(input_ids=ids, use_cache=False).logits
 
 
-def _tp_worker(rank, world, port, out_dir):
+def _tp_worker(rank, world, port, out_dir, seq_par, L):
     dist = _init(rank, world, port)
     try:
         model = _tiny_model()
-        TP.shard_llama_(model, rank, world)
+        TP.shard_llama_(model, rank, world, sequence_parallel=seq_par)
         attn = model.model.layers[0].self_attn
         assert attn.q_proj.weight.shape[0] == 4 // world * 64
         assert attn.k_proj.weight.shape[0] == 2 // world * 64
-        ids, bi, bc, blk = _tiny_inputs()
+        ids, bi, bc, blk = _tiny_inputs(L)
         out = _logits(model, ids, bi, bc, blk)
+        if seq_par:
+            # L even: the forward ran sequence-parallel; odd: all-reduces.
+            assert model._sabre_sp.active == (L % world == 0)
         torch.save(out, os.path.join(out_dir, f"tp{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
-def test_tensor_parallel_gloo_world2_matches_unsharded(tmp_path):
-    ids, bi, bc, blk = _tiny_inputs()
+@pytest.mark.parametrize("seq_par,L", [(False, 320), (True, 320), (True, 317)])
+def test_tensor_parallel_gloo_world2_matches_unsharded(tmp_path, seq_par, L):
+    """Head-parallel logits equal the unsharded model's: with all-reduces, with
+    the token-wise work split over the ranks (sequence parallel, length
+    divisible by the ranks) and with an odd length (falls back to
+    all-reduces)."""
+    ids, bi, bc, blk = _tiny_inputs(L)
     ref = _logits(_tiny_model(), ids, bi, bc, blk)
     port = _free_port()
-    mp.spawn(_tp_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_tp_worker, args=(2, port, str(tmp_path), seq_par, L), nprocs=2, join=True)
     for r in range(2):
         out = torch.load(tmp_path / f"tp{r}.pt")
         torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
