@@ -466,9 +466,13 @@ __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Para
   }
 }
 
-// One CTA per (b, query head): merge the splits in index order.
+// One CTA per (b, query head): merge the splits in index order. Launched as
+// a programmatic dependent of the split kernel: it may start while the split
+// kernel's last CTAs run, and waits here until that grid has finished and its
+// partials are visible.
 template <typename T>
 __global__ void __launch_bounds__(kD) decode_combine_kernel(const Params p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int bh = blockIdx.x;
   const int b = bh / p.Hq;
   const int h = bh - b * p.Hq;
@@ -524,8 +528,19 @@ static cudaError_t launch_decode(const Params& p, int g, cudaStream_t s) {
     launch_split<T, 4>(p, bulk, s);
   else
     launch_split<T, 8>(p, bulk, s);
-  decode_combine_kernel<T><<<p.B * p.Hq, kD, 0, s>>>(p);
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.B * p.Hq);
+  cfg.blockDim = dim3(kD);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_combine_kernel<T>, p);
 }
 
 }  // namespace decode
