@@ -84,6 +84,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-only", action="store_true",
                     help="time the prefill attention kernel alone on one layer of the workload")
+    ap.add_argument("--aux-op", choices=["mask", "token", "similarity"], default=None,
+                    help="time one of the structure-side GPU paths on the workload's prompt (c1 shape)")
     ap.add_argument("--decode-op", choices=["dense", "sparse"], default=None,
                     help="time the decode attention kernel alone on one layer of the workload: over every cached "
                          "block (dense) or over the last prompt row's list plus the generated blocks (sparse)")
@@ -337,6 +339,8 @@ def run_ours(args, rank, world, dist):
     arch, prompts, scaling = workload(args.workload, rank, world)
     if args.decode_op:
         return run_decode_op(args, rank, world, dist)
+    if args.aux_op:
+        return run_aux_op(args, rank, world, dist)
     if arch is None or args.attn_only:
         return run_op_bench(args, rank, world, dist)
     mask, topk = mask_cfg(args.workload)
@@ -609,6 +613,161 @@ def run_op_bench(args, rank, world, dist):
                                        "achieved": flop / ms / 1e9, "peak": burst, "unit": "TFLOP/s",
                                        "frac": flop / ms / 1e9 / burst, "peak_kind": f"{which} bf16 dense, burst",
                                        "flop_per_launch": flop, "ms_per_launch": ms, "traffic": traffic}}))
+
+
+def _events_ms(fn, steps, warmup):
+    """Mean device time of fn() over `steps` calls (CUDA events on the current stream)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(steps):
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        tot += s.elapsed_time(e)
+    return tot / steps
+
+
+def _token_rule_from_spans(spans, mask):
+    """Per-token arrays of the token-level rule for seeded spans (chunk,
+    same-chunk group, global flag, dependency bits), as the builder derives
+    them from text (prefix/suffix/import/signature tokens global)."""
+    import numpy as np
+    L = spans.seq_len
+    t2c = spans.token_to_chunk().astype(np.int32)
+    n = len(spans.spans)
+    glob = spans.signature_token_mask().astype(bool)
+    imp = np.zeros(max(n, 1), bool)
+    for c in spans.import_chunks:
+        imp[c] = True
+    glob |= (t2c >= 0) & imp[np.clip(t2c, 0, max(n - 1, 0))]
+    glob[:min(mask["num_prefix_tokens"], L)] = True
+    glob[max(0, L - mask["num_suffix_tokens"]):] = True
+    bpg = max(1, mask["max_chunk_tokens"] // 64)
+    gidx = (np.arange(L) // 64) // bpg
+    grp = (t2c.astype(np.int64) * (int(gidx.max()) + 2) + gidx).astype(np.int32)
+    words = max((n + 31) // 32, 1)
+    dep = np.zeros((max(n, 1), words), np.uint32)
+    ptr, idx = spans.deps_csr()
+    for a in range(n):
+        for t in idx[ptr[a]:ptr[a + 1]]:
+            dep[a, int(t) >> 5] |= np.uint32(1 << (int(t) & 31))
+    return t2c, grp, glob.astype(np.uint8), dep, n
+
+
+def run_aux_op(args, rank, world, dist):
+    """Device time of a structure-side GPU path on the workload's prompt (one
+    layer's c1 shape: 16 heads, 12288 tokens, block 64):
+      mask        block mask (R0-R3) + index lists from token-level structure;
+      token       token-level variant: block lists and per-block 64x64 masks
+                  from the token rule, then the token-mask prefill kernel;
+      similarity  chunk vectors (mean of 2048-wide bf16 embedding rows of the
+                  chunk's tokens, up to 256) and each chunk's 8 most similar
+                  chunks.
+    The CPU leg times the oracle's restatement of the same step on a bounded
+    sample (the whole step for mask/similarity, token rule at 2048 tokens)."""
+    import numpy as np
+    import torch
+    from oracle import mask_oracle as MO
+    from sabrecoder_b200 import kernels as K
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+    from sabrecoder_b200.spans import BENCH_SPAN_MIX, make_spans
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    H, L, _ = OP_SHAPES["c1"]
+    spans = make_spans(L, 1000 + rank, **BENCH_SPAN_MIX)
+    mb = StructureAwareMaskBuilder(None, **MASK)
+    info, cpu = {}, None
+    if args.aux_op == "mask":
+        ptr, idx = spans.deps_csr()
+        flags = np.asarray([1 if s.tag == "import" else 0 for s in spans.spans], np.uint8)
+        d = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in
+             dict(t2c=spans.token_to_chunk(), flags=flags, ptr=ptr, idx=idx, gtm=spans.signature_token_mask()).items()}
+
+        def fn():
+            bits, dense = mb.build_block_mask_tokens(d["t2c"], d["flags"], d["ptr"], d["idx"], d["gtm"], L, dev)
+            K.indices_from_bits(bits, dense.shape[0])
+        ms = _events_ms(fn, args.steps, args.warmup)
+        t0 = time.perf_counter()
+        MO.build_block_mask_tokens(spans.token_to_chunk(), len(spans.spans), spans.import_chunks, spans.deps,
+                                   spans.signature_token_mask(), seq_len=L, **MASK)
+        cpu = time.perf_counter() - t0
+        value, unit, metric = ms * 1e3, "us", "block mask + index lists latency (one prompt)"
+        info = {"chunks": len(spans.spans)}
+    elif args.aux_op == "token":
+        t2c, grp, glob, dep, n = _token_rule_from_spans(spans, MASK)
+        up = lambda a, dt: torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(dev)
+        tc, tg, tgl = up(t2c, torch.int32), up(grp, torch.int32), up(glob, torch.uint8)
+        db = up(dep.view(np.int32), torch.int32)
+        w = MASK["window_size"]
+        built = {}
+
+        def build():
+            bits = K.token_block_mask(tc, tg, tgl, db, n, w)
+            nb = bits.shape[0]
+            idx, cnt, mx = K.indices_from_bits(bits, nb)
+            lists = idx[:, :max(int(mx.item()), 1)].contiguous()
+            built["l"], built["c"] = lists, cnt
+            built["m"] = K.token_tile_masks(tc, tg, tgl, db, n, w, lists, cnt)
+        ms_build = _events_ms(build, args.steps, args.warmup)
+        g = torch.Generator(device=dev).manual_seed(rank)
+        q, k, v = (torch.randn(1, L, H, 128, device=dev, generator=g, dtype=torch.bfloat16).transpose(1, 2)
+                   for _ in range(3))
+        bi, bc = built["l"][None], built["c"][None]
+        out = torch.empty_like(q)
+        flush = L2Flush(dev)
+
+        def attn():
+            flush()
+            K.prefill_bsa(q, k, v, bi, bc, 64, out=out, token_masks=built["m"])
+        ms_attn = _events_ms(attn, args.steps, args.warmup)
+        ms_flush = _events_ms(flush, args.steps, 1)
+        ms_attn = max(ms_attn - ms_flush, 1e-6)
+        flop = float(bc.sum().item()) * H * 4 * 64 * 64 * 128
+        Ls = 2048
+        sp = make_spans(Ls, 1000 + rank, **BENCH_SPAN_MIX)
+        t0 = time.perf_counter()
+        MO.token_level_mask_tokens(sp.token_to_chunk(), len(sp.spans), sp.import_chunks, sp.deps,
+                                   sp.signature_token_mask(), seq_len=Ls, **MASK)
+        cpu = (time.perf_counter() - t0) * (L / Ls) ** 2  # O(L^2): scaled to the full prompt
+        value, unit, metric = ms_build * 1e3, "us", "token-level lists + 64x64 masks latency (one prompt)"
+        info = {"prefill_token_mode_tflops": flop / ms_attn / 1e9, "prefill_ms": ms_attn,
+                "listed_pairs": int(bc.sum().item()), "density": float(bc.sum().item()) / (
+                    (L // 64) * (L // 64 + 1) / 2)}
+    else:
+        n_chunks = len(spans.spans)
+        ids = np.random.default_rng(rank).integers(0, 32256, size=L).astype(np.int32)
+        tok_lists = [ids[s.start:s.end + 1][:256] for s in spans.spans]
+        ptr = np.concatenate([[0], np.cumsum([len(t) for t in tok_lists])]).astype(np.int32)
+        flat = np.concatenate(tok_lists).astype(np.int32)
+        emb = (torch.randn(32256, 2048, generator=torch.Generator().manual_seed(5)) * 0.02).to(torch.bfloat16).to(dev)
+        dptr, dflat = torch.from_numpy(ptr).to(dev), torch.from_numpy(flat).to(dev)
+        rows = torch.arange(n_chunks, dtype=torch.int32, device=dev)
+        kk = min(8, int(n_chunks * 0.1))
+
+        def fn():
+            vecs = K.chunk_vectors(emb, dptr, dflat)
+            K.similarity_topk(vecs, rows, rows, rows, rows, kk)
+        ms = _events_ms(fn, args.steps, args.warmup)
+        e32 = emb.float().cpu().numpy()
+        t0 = time.perf_counter()
+        vec = MO.chunk_vectors_f16(e32, [t.tolist() for t in tok_lists])
+        MO.similarity_topk(vec, list(range(n_chunks)), list(range(n_chunks)), list(range(n_chunks)),
+                           list(range(n_chunks)), kk)
+        cpu = time.perf_counter() - t0
+        value, unit, metric = ms * 1e3, "us", "chunk-similarity vectors + top-k latency (one prompt)"
+        info = {"chunks": n_chunks, "k": kk, "embedding": "32256 x 2048 bf16"}
+    if rank == 0:
+        print(json.dumps({"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps,
+                          "warmup": args.warmup, "ms_per_step": value / 1e3, "higher_is_better": False,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "int32/bf16", "data": "synthetic",
+                          "config": {"workload": f"{args.aux_op} on the c1 prompt (12288 tokens, 16 heads, block 64)",
+                                     **info},
+                          "cpu_baseline": {"value": cpu * 1e6, "unit": "us", "cores": 1, "kind": "port",
+                                           "sample": "the oracle's restatement on the host"}}))
 
 
 DECODE_SHAPES = {"c0": (16, 4096, 64), "c1": (16, 12288, 64), "c2": (16, 16384, 64), "c3": (32, 16384, 128)}

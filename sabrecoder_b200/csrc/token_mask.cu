@@ -53,52 +53,50 @@ __device__ __forceinline__ unsigned long long row_word(const TokenRule& r, int i
   return w;
 }
 
-// One CTA (64 threads, thread = query row) per query block: bit kb of
-// row_bits[qb] is set when any pair of (qb, kb) is visible.
-__global__ void __launch_bounds__(kB) token_block_rows_kernel(const TokenRule r, uint32_t* row_bits, int nwords) {
+// Key block kb's per-token data into shared memory (thread t: token kb*64+t).
+__device__ __forceinline__ void load_key_block(const TokenRule& r, int kb, int t, int32_t* s_chunk,
+                                               int32_t* s_group, uint8_t* s_global) {
+  const int j = kb * kB + t;
+  s_chunk[t] = j < r.L ? r.chunk[j] : -1;
+  s_group[t] = j < r.L ? r.group[j] : 0;
+  s_global[t] = j < r.L ? r.global[j] : 0;
+}
+
+// One CTA (64 threads, thread = query row) per (key block, query block) pair
+// with kb <= qb: bit kb of row_bits[qb] is set when any of its pairs is
+// visible. row_bits starts zeroed. The pairs are independent, so the
+// triangle of work spreads over the whole GPU.
+__global__ void __launch_bounds__(kB) token_block_pairs_kernel(const TokenRule r, uint32_t* row_bits, int nwords) {
   __shared__ int32_t s_chunk[kB];
   __shared__ int32_t s_group[kB];
   __shared__ uint8_t s_global[kB];
-  const int qb = blockIdx.x;
+  const int kb = blockIdx.x;
+  const int qb = blockIdx.y;
+  if (kb > qb) return;
   const int t = threadIdx.x;
-  const int i = qb * kB + t;
-  for (int w = t; w < nwords; w += kB) row_bits[static_cast<long long>(qb) * nwords + w] = 0u;
-  for (int kb = 0; kb <= qb; ++kb) {
-    __syncthreads();
-    const int j = kb * kB + t;
-    s_chunk[t] = j < r.L ? r.chunk[j] : -1;
-    s_group[t] = j < r.L ? r.group[j] : 0;
-    s_global[t] = j < r.L ? r.global[j] : 0;
-    __syncthreads();
-    const unsigned long long wd = row_word(r, i, kb, s_chunk, s_group, s_global);
-    if (__syncthreads_or(wd != 0ull) && t == 0)
-      row_bits[static_cast<long long>(qb) * nwords + (kb >> 5)] |= 1u << (kb & 31);
-  }
+  load_key_block(r, kb, t, s_chunk, s_group, s_global);
+  __syncthreads();
+  const unsigned long long wd = row_word(r, qb * kB + t, kb, s_chunk, s_group, s_global);
+  if (__syncthreads_or(wd != 0ull) && t == 0)
+    atomicOr(&row_bits[static_cast<long long>(qb) * nwords + (kb >> 5)], 1u << (kb & 31));
 }
 
-// One CTA per query block: the 64 row words of every listed key block, in
-// list order, at masks[(row_ptr[qb] + i) * 64 + row].
+// One CTA per listed (query block, list entry): the 64 row words of that key
+// block at masks[(row_ptr[qb] + e) * 64 + row].
 __global__ void __launch_bounds__(kB) token_tile_masks_kernel(const TokenRule r, const int32_t* indices, int cap,
                                                              const int32_t* counts, const int32_t* row_ptr,
                                                              unsigned long long* masks) {
   __shared__ int32_t s_chunk[kB];
   __shared__ int32_t s_group[kB];
   __shared__ uint8_t s_global[kB];
-  const int qb = blockIdx.x;
+  const int e = blockIdx.x;
+  const int qb = blockIdx.y;
+  if (e >= counts[qb]) return;
   const int t = threadIdx.x;
-  const int i = qb * kB + t;
-  const int n = counts[qb];
-  const long long base = row_ptr[qb];
-  for (int e = 0; e < n; ++e) {
-    const int kb = indices[static_cast<long long>(qb) * cap + e];
-    __syncthreads();
-    const int j = kb * kB + t;
-    s_chunk[t] = j < r.L ? r.chunk[j] : -1;
-    s_group[t] = j < r.L ? r.group[j] : 0;
-    s_global[t] = j < r.L ? r.global[j] : 0;
-    __syncthreads();
-    masks[(base + e) * kB + t] = row_word(r, i, kb, s_chunk, s_group, s_global);
-  }
+  const int kb = indices[static_cast<long long>(qb) * cap + e];
+  load_key_block(r, kb, t, s_chunk, s_group, s_global);
+  __syncthreads();
+  masks[(row_ptr[qb] + static_cast<long long>(e)) * kB + t] = row_word(r, qb * kB + t, kb, s_chunk, s_group, s_global);
 }
 
 }  // namespace tokmask
@@ -115,6 +113,8 @@ static int token_rule(sabre::tokmask::TokenRule* r, const int32_t* tok_chunk, co
     return sabre_fail(SABRE_ERR_INVALID_ARG, "%s: null pointer argument", who);
   if (seq_len <= 0 || nchunks < 0 || window < 0)
     return sabre_fail(SABRE_ERR_INVALID_ARG, "%s: bad sizes", who);
+  if ((seq_len + 63) / 64 > 65535)
+    return sabre_fail(SABRE_ERR_UNSUPPORTED, "%s: seq_len %d > %d", who, seq_len, 65535 * 64);
   r->chunk = tok_chunk;
   r->group = tok_group;
   r->global = tok_global;
@@ -136,8 +136,12 @@ int sabre_token_block_mask(const int32_t* tok_chunk, const int32_t* tok_group, c
   if (st != SABRE_OK) return st;
   if (!row_bits) return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_token_block_mask: null row_bits");
   const int nb = (seq_len + kB - 1) / kB;
-  token_block_rows_kernel<<<nb, kB, 0, static_cast<cudaStream_t>(stream)>>>(r, row_bits, (nb + 31) / 32);
-  cudaError_t e = cudaGetLastError();
+  const int nwords = (nb + 31) / 32;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(row_bits, 0, static_cast<size_t>(nb) * nwords * sizeof(uint32_t), s);
+  if (e != cudaSuccess) return sabre_cuda_fail(e, "sabre_token_block_mask memset");
+  token_block_pairs_kernel<<<dim3(nb, nb), kB, 0, s>>>(r, row_bits, nwords);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return sabre_cuda_fail(e, "sabre_token_block_mask launch");
   return SABRE_OK;
 }
@@ -153,7 +157,7 @@ int sabre_token_tile_masks(const int32_t* tok_chunk, const int32_t* tok_group, c
   if (!indices || !counts || !row_ptr || !masks || cap <= 0)
     return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_token_tile_masks: null list or output");
   const int nb = (seq_len + kB - 1) / kB;
-  token_tile_masks_kernel<<<nb, kB, 0, static_cast<cudaStream_t>(stream)>>>(
+  token_tile_masks_kernel<<<dim3(cap, nb), kB, 0, static_cast<cudaStream_t>(stream)>>>(
       r, indices, cap, counts, row_ptr, reinterpret_cast<unsigned long long*>(masks));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return sabre_cuda_fail(e, "sabre_token_tile_masks launch");
