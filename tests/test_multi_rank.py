@@ -130,7 +130,15 @@ def _logits(model, ids, bi, bc, blk):
         return model(input_ids=ids, use_cache=False).logits
 
 
-def _tp_worker(rank, world, port, out_dir, seq_par, L):
+def _batched(L, batch):
+    ids, bi, bc, blk = _tiny_inputs(L)
+    if batch == 2:  # a second, different prompt with the same lists
+        ids = torch.cat([ids, ids.flip(1)], 0)
+        bi, bc = bi.expand(2, -1, -1).contiguous(), bc.expand(2, -1).contiguous()
+    return ids, bi, bc, blk
+
+
+def _tp_worker(rank, world, port, out_dir, seq_par, L, batch):
     dist = _init(rank, world, port)
     try:
         model = _tiny_model()
@@ -138,7 +146,7 @@ def _tp_worker(rank, world, port, out_dir, seq_par, L):
         attn = model.model.layers[0].self_attn
         assert attn.q_proj.weight.shape[0] == 4 // world * 64
         assert attn.k_proj.weight.shape[0] == 2 // world * 64
-        ids, bi, bc, blk = _tiny_inputs(L)
+        ids, bi, bc, blk = _batched(L, batch)
         out = _logits(model, ids, bi, bc, blk)
         if seq_par:
             # L even: the forward ran sequence-parallel; odd: all-reduces.
@@ -148,16 +156,16 @@ def _tp_worker(rank, world, port, out_dir, seq_par, L):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("seq_par,L", [(False, 320), (True, 320), (True, 317)])
-def test_tensor_parallel_gloo_world2_matches_unsharded(tmp_path, seq_par, L):
+@pytest.mark.parametrize("seq_par,L,batch", [(False, 320, 1), (True, 320, 1), (True, 317, 1), (True, 320, 2)])
+def test_tensor_parallel_gloo_world2_matches_unsharded(tmp_path, seq_par, L, batch):
     """Head-parallel logits equal the unsharded model's: with all-reduces, with
     the token-wise work split over the ranks (sequence parallel, length
     divisible by the ranks) and with an odd length (falls back to
-    all-reduces)."""
-    ids, bi, bc, blk = _tiny_inputs(L)
+    all-reduces), for one prompt and for a batch of two."""
+    ids, bi, bc, blk = _batched(L, batch)
     ref = _logits(_tiny_model(), ids, bi, bc, blk)
     port = _free_port()
-    mp.spawn(_tp_worker, args=(2, port, str(tmp_path), seq_par, L), nprocs=2, join=True)
+    mp.spawn(_tp_worker, args=(2, port, str(tmp_path), seq_par, L, batch), nprocs=2, join=True)
     for r in range(2):
         out = torch.load(tmp_path / f"tp{r}.pt")
         torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
