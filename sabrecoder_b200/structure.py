@@ -26,11 +26,14 @@ is what this module does:
   chunk covering it; a reference goes to every other chunk of that name.
   Python classes contribute no inheritance references in the reference.
 
-Source that does not parse as a whole (a prompt cut in the middle of a
-statement) is parsed without its last lines, removed one at a time up to
-``max_trim_lines``; the removed lines become MODULE_CODE through the gap
-rule. tree-sitter instead recovers around the error, so chunks next to a
-syntax error may differ from the reference's.
+Source that does not parse as a whole is repaired locally, as tree-sitter
+recovers around an error: the line a syntax error is reported on is replaced
+by ``pass`` at its indentation and the parse retried (up to ``max_fixes``
+times; a Python 2 ``print x`` in the middle of a file then costs that line
+only). If that does not converge (a prompt cut in the middle of a
+statement), the last lines are dropped one at a time (up to
+``max_trim_lines``) and become MODULE_CODE through the gap rule. Chunks next
+to a syntax error may differ from tree-sitter's.
 """
 
 from __future__ import annotations
@@ -90,14 +93,31 @@ class _Source:
         return a, b
 
 
-def _parse(code: str, max_trim_lines: int) -> Tuple[Optional[ast.Module], int]:
+def _neutralised(lines: List[str], max_fixes: int) -> Optional[ast.Module]:
+    """Parse, replacing each line a syntax error points at by ``pass``."""
+    lines = list(lines)
+    for _ in range(max_fixes + 1):
+        try:
+            return ast.parse("\n".join(lines))
+        except SyntaxError as e:
+            ln = min(max(int(e.lineno or len(lines)), 1), len(lines))
+            body = lines[ln - 1]
+            fix = body[: len(body) - len(body.lstrip())] + "pass"
+            if body == fix:  # already neutral: the error is not local to this line
+                return None
+            lines[ln - 1] = fix
+        except ValueError:
+            return None
+    return None
+
+
+def _parse(code: str, max_trim_lines: int, max_fixes: int = 64) -> Tuple[Optional[ast.Module], int]:
     """(module, number of trailing lines dropped to make it parse)."""
     lines = code.split("\n")
     for drop in range(0, min(max_trim_lines, len(lines) - 1) + 1):
-        try:
-            return ast.parse("\n".join(lines[: len(lines) - drop]) if drop else code), drop
-        except (SyntaxError, ValueError):
-            continue
+        tree = _neutralised(lines[: len(lines) - drop], max_fixes if drop == 0 else 0)
+        if tree is not None:
+            return tree, drop
     return None, 0
 
 

@@ -59,14 +59,28 @@ def test_language_detection_and_non_python():
 
 
 def test_truncated_source_keeps_the_parsed_prefix():
-    """A prompt cut inside a statement: the lines that do not parse become a
-    MODULE_CODE chunk, the definitions before them keep their chunks."""
+    """A prompt cut inside a statement: the line the error is on is
+    neutralised, so the definitions around it keep their chunks and their
+    references."""
     code = "import os\n\ndef f(x):\n    return g(x)\n\ndef g(y):\n    return (y +\n"
     chunks = PythonSegmenter().segment_code(code)
     kinds = [(c.chunk_type.name, c.start_line, c.end_line) for c in chunks]
-    assert kinds == [("MODULE_CODE", 5, 8), ("IMPORT", 1, 2), ("FUNCTION", 3, 4)]
+    assert kinds == [("IMPORT", 1, 2), ("FUNCTION", 3, 5), ("FUNCTION", 6, 8)]
     refs = PythonReferenceAnalyzer(chunks, code).analyze()
-    assert refs == []  # g's definition is in the unparsed tail, so no chunk is named g
+    assert [(r.source_chunk_idx, r.target_chunk_idx, r.name) for r in refs] == [(1, 2, "g")]
+
+
+def test_syntax_errors_cost_only_their_lines():
+    """Python 2 print statements inside and between definitions: every
+    definition still becomes a chunk, and calls elsewhere are still found."""
+    code = ("import os\n\ndef f(x):\n    print 'hi'\n    return g(x)\n\nprint x\n\nclass K:\n"
+            "    def m(self):\n        return f(1)\n\ndef g(y):\n    return y\n")
+    chunks = PythonSegmenter().segment_code(code)
+    got = [(c.chunk_type.name, c.name, c.start_line, c.end_line) for c in chunks]
+    assert got == [("MODULE_CODE", "", 6, 8), ("IMPORT", "import", 1, 2), ("FUNCTION", "f", 3, 5),
+                   ("CLASS", "K", 9, 12), ("METHOD", "m", 10, 11), ("FUNCTION", "g", 13, 15)]
+    refs = PythonReferenceAnalyzer(chunks, code).analyze()
+    assert sorted((r.source_chunk_idx, r.target_chunk_idx, r.name) for r in refs) == [(2, 5, "g"), (4, 2, "f")]
 
 
 def test_builder_uses_builtin_structure_without_tree_sitter():
