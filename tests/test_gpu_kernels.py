@@ -259,7 +259,11 @@ def test_pooled_topk_bit_exact(K, B, Hq, Hkv, L, block, topk):
 
 @pytest.mark.parametrize("B,Hq,Hkv,Tmax,block,shared", [(1, 4, 4, 3000, 64, True), (2, 7, 1, 2048, 128, False),
                                                          (3, 8, 2, 1500, 64, False), (1, 2, 2, 64, 64, True),
-                                                         (1, 16, 2, 5000, 64, False), (2, 4, 4, 700, 192, True)])
+                                                         (1, 16, 2, 5000, 64, False), (2, 4, 4, 700, 192, True),
+                                                         # 9 or more (sequence, KV head) groups: the splits of a
+                                                         # group merge inside one thread-block cluster
+                                                         (1, 16, 16, 3000, 64, False), (2, 32, 8, 2000, 64, True),
+                                                         (3, 24, 3, 1800, 128, False), (1, 32, 32, 4100, 64, True)])
 def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
     gen = torch.Generator().manual_seed(Tmax + Hq)
     D = 128
