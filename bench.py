@@ -770,13 +770,16 @@ def run_aux_op(args, rank, world, dist):
                                            "sample": "the oracle's restatement on the host"}}))
 
 
-DECODE_SHAPES = {"c0": (16, 4096, 64), "c1": (16, 12288, 64), "c2": (16, 16384, 64), "c3": (32, 16384, 128)}
+# (query heads, KV heads, prompt tokens, generated tokens) of one layer on one GPU.
+DECODE_SHAPES = {"c0": (16, 16, 4096, 64), "c1": (16, 16, 12288, 64), "c2": (16, 16, 16384, 64),
+                 "c3": (32, 32, 16384, 128), "c4": (56, 8, 16384, 64)}
 
 
 def run_decode_op(args, rank, world, dist):
     """The decode attention op alone on one layer's shape of the workload: one
     query row per head after a prompt of L tokens and `gen` generated tokens
-    (c1: H=16, L=12288, 64 generated; c3: H=32, L=16384, 128 generated), K/V
+    (c1: H=16, L=12288, 64 generated; c3: H=32, L=16384, 128 generated; c4:
+    56 query heads over 8 KV heads, L=16384, block 128, 64 generated), K/V
     cache in HBM, L2 flushed between timed launches. Bytes counted are the K
     and V rows of the listed blocks (plus q and o)."""
     import torch
@@ -784,27 +787,29 @@ def run_decode_op(args, rank, world, dist):
     from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
     from sabrecoder_b200.spans import BENCH_SPAN_MIX, make_spans
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
-    H, L, gen = DECODE_SHAPES[args.workload]
-    blk = MASK["block_size"]
+    Hq, H, L, gen = DECODE_SHAPES[args.workload]
+    mask, _ = mask_cfg(args.workload)
+    blk = mask["block_size"]
     T = L + gen
     g = torch.Generator(device=dev).manual_seed(rank)
     kc = torch.randn(1, H, T, 128, device=dev, generator=g, dtype=torch.bfloat16)
     vc = torch.randn(1, H, T, 128, device=dev, generator=g, dtype=torch.bfloat16)
-    q = torch.randn(1, H, 128, device=dev, generator=g, dtype=torch.bfloat16)
+    q = torch.randn(1, Hq, 128, device=dev, generator=g, dtype=torch.bfloat16)
     nbk = (T + blk - 1) // blk
     if args.decode_op == "dense":
         lst = torch.arange(nbk, device=dev, dtype=torch.int32).unsqueeze(0)
         cnt = torch.tensor([nbk], dtype=torch.int32, device=dev)
     else:
-        mb = StructureAwareMaskBuilder(None, **MASK)
-        bi, bc, _ = mb.build_block_indices_from_spans(make_spans(L, 1000 + rank, **BENCH_SPAN_MIX), dev)
+        mb = StructureAwareMaskBuilder(None, **mask)
+        mix = C4_SPAN_MIX if mask is MASK_C4 else BENCH_SPAN_MIX
+        bi, bc, _ = mb.build_block_indices_from_spans(make_spans(L, 1000 + rank, **mix), dev)
         nb_p = (L + blk - 1) // blk
         c_last = int(bc[0, nb_p - 1].item())
         lst = torch.cat([bi[0, nb_p - 1, :c_last].to(torch.int32),
                          torch.arange(nb_p, nbk, device=dev, dtype=torch.int32)]).unsqueeze(0).contiguous()
         cnt = torch.tensor([lst.shape[1]], dtype=torch.int32, device=dev)
     seq = torch.tensor([T], dtype=torch.int32, device=dev)
-    ws = torch.empty(K.decode_workspace_bytes(1, H, H, 128, lst.shape[1]), dtype=torch.uint8, device=dev)
+    ws = torch.empty(K.decode_workspace_bytes(1, Hq, H, 128, lst.shape[1]), dtype=torch.uint8, device=dev)
     out = torch.empty_like(q)
     flush = L2Flush(dev)
     for _ in range(max(3, args.warmup)):
@@ -835,7 +840,7 @@ def run_decode_op(args, rank, world, dist):
     rows = 0
     for kb in lst[0, :int(cnt.item())].tolist():
         rows += max(0, min(blk, T - kb * blk))
-    nbytes = rows * H * 128 * 2 * 2 + 2 * H * 128 * 2
+    nbytes = rows * H * 128 * 2 * 2 + 2 * Hq * 128 * 2
     gbs = nbytes / ms / 1e6
     _, _, hbm, which = measured_peaks()
     traffic = profile_traffic(f"decode_bsa_{args.workload}_{args.decode_op}")
@@ -844,7 +849,7 @@ def run_decode_op(args, rank, world, dist):
                           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                           "data": "synthetic",
-                          "config": {"workload": f"{args.workload} decode op: B=1 H={H} cache {T} tokens D=128 "
+                          "config": {"workload": f"{args.workload} decode op: B=1 Hq={Hq} Hkv={H} cache {T} tokens D=128 "
                                                  f"block {blk}, {args.decode_op} list of {int(cnt.item())} blocks",
                                      "l2": L2Flush.NOTE},
                           "roofline": {"kernel": "sabre decode_split_kernel + decode_combine_kernel",

@@ -503,6 +503,16 @@ static void launch_split(const Params& p, bool bulk, cudaStream_t s) {
     decode_split_kernel<T, G><<<grid, kThreads, 0, s>>>(p);
 }
 
+// Groups of at least this many query heads per KV head decode on the tensor
+// cores (decode_gqa.cu, defined later in this translation unit): scoring a
+// row against that many heads costs the CUDA-core kernels more than reading
+// it. The tiles there are 64 rows, so blocks must be multiples of 64.
+constexpr int kGqaMinGroup = 3;
+static int decode_gqa_launch(const Params& p, int dtype, cudaStream_t s);
+static bool use_gqa(const Params& p) {
+  return p.Hq / p.Hkv >= kGqaMinGroup && p.block % kChunkRows == 0;
+}
+
 // Bulk streaming needs rows contiguous per head and whole 64-row chunks per
 // block; other layouts use the register-streaming kernel.
 static bool bulk_layout(const Params& p) {
@@ -627,6 +637,7 @@ int sabre_decode_bsa(const void* q, const void* k_cache, const void* v_cache, vo
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int g = heads_q / heads_kv;
+  if (use_gqa(p)) return decode_gqa_launch(p, dtype, s);
   cudaError_t e;
   if (dtype == SABRE_BF16)
     e = launch_decode<__nv_bfloat16>(p, g, s);
@@ -778,6 +789,7 @@ int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_c
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int g = heads_q / heads_kv;
+  if (use_gqa(p)) return decode_gqa_launch(p, dtype, s);
   cudaError_t e;
   if (dtype == SABRE_BF16)
     e = launch_decode<__nv_bfloat16>(p, g, s);

@@ -96,6 +96,8 @@ static int ensure_smem_attr(Kern kern, int bytes) {
 
 }  // namespace sabre
 
+#include "decode_gqa.cu"
+
 using namespace sabre;
 
 extern "C" {

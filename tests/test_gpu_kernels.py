@@ -286,12 +286,14 @@ def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
     _close(out, ref)
 
 
-@pytest.mark.parametrize("block,row_pad", [(32, 0), (64, 128)])
-def test_decode_strided_cache_vs_oracle(K, block, row_pad):
+@pytest.mark.parametrize("block,row_pad,Hq", [(32, 0, 4), (64, 128, 4), (64, 128, 14), (128, 64, 16)])
+def test_decode_strided_cache_vs_oracle(K, block, row_pad, Hq):
     """Caches whose rows are not contiguous per head (row stride > head_dim) or
-    blocks that are not whole 64-row chunks take the register-streaming kernel."""
-    gen = torch.Generator().manual_seed(block + row_pad)
-    B, Hq, Hkv, Tmax, D = 2, 4, 2, 1200, 128
+    blocks that are not whole 64-row chunks take the register-streaming kernel;
+    groups of 7 and 8 query heads per KV head read the same strided caches
+    through TMA tensor maps on the tensor-core path."""
+    gen = torch.Generator().manual_seed(block + row_pad + Hq)
+    B, Hkv, Tmax, D = 2, 2, 1200, 128
     q = torch.randn(B, Hq, D, generator=gen).to(torch.bfloat16)
     kbig = torch.randn(B, Hkv, Tmax, D + row_pad, generator=gen).to(torch.bfloat16)
     vbig = torch.randn(B, Hkv, Tmax, D + row_pad, generator=gen).to(torch.bfloat16)
