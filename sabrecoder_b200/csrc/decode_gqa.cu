@@ -71,13 +71,22 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int b = blockIdx.z;
   const int g = p.Hq / p.Hkv;
 
+  // The start-up global loads are independent and issued together: the
+  // sequence length, the list count, the split's first index (prefetched for
+  // the producers' list walks) and this thread's 16 bytes of Q.
+  const int T_valid = min(p.seq_lens[b], p.Tmax);
+  int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];
+  const int j0 = split * p.bps;
+  const int32_t* ip = p.idx + b * p.idx_sb + hk * p.idx_sh;
+  if (tid == 32 && j0 < p.max_active) asm volatile("prefetch.global.L1 [%0];" ::"l"(ip + j0 * p.idx_sk));
   // Q: row r < g is query head hk*g + r, stored as the 128-byte-swizzled
   // K-major layout a TMA load would produce (16-byte chunk c of row r of a
   // d-half at r*128 + ((c ^ (r & 7)) << 4)); rows g..7 are zero.
-  for (int i = tid; i < 2 * 8 * 8; i += kThreads) {
-    const int c = i & 7;
-    const int r = (i >> 3) & 7;
-    const int dh = i >> 6;
+  static_assert(2 * 8 * 8 == kThreads, "one 16-byte chunk of Q per thread");
+  {
+    const int c = tid & 7;
+    const int r = (tid >> 3) & 7;
+    const int dh = tid >> 6;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (r < g) {
       const T* qp = static_cast<const T*>(p.q) + b * p.q_sb + (hk * g + r) * p.q_sh + dh * 64 + c * 8;
@@ -117,12 +126,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem = *tmem_slot;
   const bool start_ok = (*abort_flag == 0);
 
-  const int T_valid = min(p.seq_lens[b], p.Tmax);
-  int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];
   cnt = min(cnt, p.max_active);
-  const int j0 = split * p.bps;
   const int j1 = min(j0 + p.bps, cnt);
-  const int32_t* ip = p.idx + b * p.idx_sb + hk * p.idx_sh;
 
   constexpr uint32_t kIdescQK = idesc_f16(128, 64, DT<T>::kBf16, false);
   constexpr uint32_t kIdescPV = idesc_f16(128, 128, DT<T>::kBf16, true);
