@@ -118,7 +118,8 @@ def _tiny_llama(H, Hkv, layers=2, vocab=512, init=0.08, seed=0):
     return LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
 
 
-@pytest.mark.parametrize("H,Hkv", [(2, 2), (4, 2)])
+# (8, 2): four query heads per KV head decode on the tensor-core path.
+@pytest.mark.parametrize("H,Hkv", [(2, 2), (4, 2), (8, 2)])
 def test_patched_llama_greedy_tokens_match_oracle(cuda, H, Hkv):
     """Sparse prefill + 32 dense decode steps of a patched 2-layer model
     against the oracle model on the same bf16 weights, in lockstep: both
