@@ -470,23 +470,39 @@ __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Para
 // a programmatic dependent of the split kernel: it may start while the split
 // kernel's last CTAs run, and waits here until that grid has finished and its
 // partials are visible.
+// The (m, l) of all splits are read in one parallel pass into shared memory
+// and each thread's acc values in independent groups of 8, so the loads do
+// not wait on one another; the sums run in split order as before.
 template <typename T>
 __global__ void __launch_bounds__(kD) decode_combine_kernel(const Params p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float sm_m[kMaxSplits], sm_l[kMaxSplits];
   const int bh = blockIdx.x;
   const int b = bh / p.Hq;
   const int h = bh - b * p.Hq;
   const int d = threadIdx.x;
   const long long base = static_cast<long long>(bh) * p.splits;
+  for (int s = d; s < p.splits; s += kD) {
+    sm_m[s] = p.part_ml[(base + s) * 2];
+    sm_l[s] = p.part_ml[(base + s) * 2 + 1];
+  }
+  __syncthreads();
   float M = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.part_ml[(base + s) * 2]);
+  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, sm_m[s]);
   float L = 0.f, A = 0.f;
   if (M != -INFINITY) {
-    for (int s = 0; s < p.splits; ++s) {
-      const float ms = p.part_ml[(base + s) * 2];
-      const float w = ex2(ms - M);
-      L += w * p.part_ml[(base + s) * 2 + 1];
-      A += w * p.part_acc[(base + s) * kD + d];
+    for (int s0 = 0; s0 < p.splits; s0 += 8) {
+      float a[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] = (s0 + u < p.splits) ? p.part_acc[(base + s0 + u) * kD + d] : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (s0 + u < p.splits) {
+          const float w = ex2(sm_m[s0 + u] - M);
+          L += w * sm_l[s0 + u];
+          A += w * a[u];
+        }
+      }
     }
   }
   const float out = (L > 0.f) ? A / L : 0.f;
