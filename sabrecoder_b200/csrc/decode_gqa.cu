@@ -313,11 +313,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int c = 0; c < 32; ++c) ov[c] = 0u;
         }
         if (real) {
-          float4* dst = reinterpret_cast<float4*>(p.part_acc + slot * kD + ch * 32);
+          // 4-byte stores: the caller's workspace need only be float-aligned.
+          float* dst = p.part_acc + slot * kD + ch * 32;
 #pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4)
-            dst[q4] = make_float4(__uint_as_float(ov[4 * q4]), __uint_as_float(ov[4 * q4 + 1]),
-                                  __uint_as_float(ov[4 * q4 + 2]), __uint_as_float(ov[4 * q4 + 3]));
+          for (int c = 0; c < 32; ++c) dst[c] = __uint_as_float(ov[c]);
         }
       }
       if (real) {
