@@ -63,7 +63,9 @@ def test_noalloc_decode_matches_workspace_decode_on_two_calls():
         pytest.skip("no CUDA device")
     from sabrecoder_b200 import kernels as K
     dev = torch.device("cuda")
-    for seed, shape in ((1, (2, 8, 2, 3000, 64)), (2, (1, 7, 1, 2100, 128))):
+    # Groups of 4 and 7 query heads per KV head take the tensor-core decode,
+    # one head per KV head the CUDA-core one.
+    for seed, shape in ((1, (2, 8, 2, 3000, 64)), (2, (1, 7, 1, 2100, 128)), (3, (3, 4, 4, 1800, 64))):
         B, Hq, Hkv, Tmax, block = shape
         q, kc, vc, idx, cnt, seq = _case(seed, B, Hq, Hkv, Tmax, block, dev)
         ref = K.decode_bsa(q, kc, vc, idx, cnt, seq, block)
