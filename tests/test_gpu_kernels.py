@@ -263,7 +263,9 @@ def test_pooled_topk_bit_exact(K, B, Hq, Hkv, L, block, topk):
                                                          # 9 or more (sequence, KV head) groups: the splits of a
                                                          # group merge inside one thread-block cluster
                                                          (1, 16, 16, 3000, 64, False), (2, 32, 8, 2000, 64, True),
-                                                         (3, 24, 3, 1800, 128, False), (1, 32, 32, 4100, 64, True)])
+                                                         (3, 24, 3, 1800, 128, False), (1, 32, 32, 4100, 64, True),
+                                                         # a cache shorter than one 64-row tile
+                                                         (2, 8, 2, 40, 64, False)])
 def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
     gen = torch.Generator().manual_seed(Tmax + Hq)
     D = 128
