@@ -288,6 +288,28 @@ def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
     _close(out, ref)
 
 
+@pytest.mark.parametrize("Hq,Hkv", [(4, 4), (8, 2)])
+def test_decode_f16_vs_oracle(K, Hq, Hkv):
+    """fp16 caches: one query head per KV head (CUDA-core kernel) and four
+    (tensor-core kernel)."""
+    gen = torch.Generator().manual_seed(99 + Hq)
+    B, Tmax, block, D = 2, 1500, 64, 128
+    q = torch.randn(B, Hq, D, generator=gen).to(torch.float16)
+    kc = torch.randn(B, Hkv, Tmax, D, generator=gen).to(torch.float16)
+    vc = torch.randn(B, Hkv, Tmax, D, generator=gen).to(torch.float16)
+    seq = torch.tensor([Tmax, 901], dtype=torch.int32)
+    nbk = (Tmax + block - 1) // block
+    m = torch.rand(B, Hkv, nbk, generator=gen) < 0.4
+    for b in range(B):
+        m[b, :, (int(seq[b]) - 1) // block] = True
+    idx, cnt = MO.block_indices_from_mask(m.numpy())
+    bi, bc = torch.from_numpy(idx), torch.from_numpy(cnt)
+    out = K.decode_bsa(q.cuda(), kc.cuda(), vc.cuda(), bi.cuda(), bc.cuda(), seq.cuda(), block)
+    torch.cuda.synchronize()
+    ref = AO.sparse_decode_fp32(q, kc, vc, bi, bc, seq, block)
+    _close(out, ref)
+
+
 @pytest.mark.parametrize("block,row_pad,Hq", [(32, 0, 4), (64, 128, 4), (64, 128, 14), (128, 64, 16)])
 def test_decode_strided_cache_vs_oracle(K, block, row_pad, Hq):
     """Caches whose rows are not contiguous per head (row stride > head_dim) or
