@@ -86,7 +86,7 @@ def parse_args():
                     help="time the prefill attention kernel alone on one layer of the workload")
     ap.add_argument("--aux-op", choices=["mask", "token", "similarity"], default=None,
                     help="time one of the structure-side GPU paths on the workload's prompt (c1 shape)")
-    ap.add_argument("--decode-op", choices=["dense", "sparse"], default=None,
+    ap.add_argument("--decode-op", choices=["dense", "sparse", "qkv"], default=None,
                     help="time the decode attention kernel alone on one layer of the workload: over every cached "
                          "block (dense) or over the last prompt row's list plus the generated blocks (sparse)")
     return ap.parse_args()
@@ -337,6 +337,8 @@ def run_ours(args, rank, world, dist):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     arch, prompts, scaling = workload(args.workload, rank, world)
+    if args.decode_op == "qkv":
+        return run_qkv_op(args, rank, world, dist)
     if args.decode_op:
         return run_decode_op(args, rank, world, dist)
     if args.aux_op:
@@ -773,6 +775,85 @@ def run_aux_op(args, rank, world, dist):
 # (query heads, KV heads, prompt tokens, generated tokens) of one layer on one GPU.
 DECODE_SHAPES = {"c0": (16, 16, 4096, 64), "c1": (16, 16, 12288, 64), "c2": (16, 16, 16384, 64),
                  "c3": (32, 32, 16384, 128), "c4": (56, 8, 16384, 64)}
+
+
+# hidden size of each workload's model (query / KV heads come from DECODE_SHAPES).
+HIDDEN = {"c0": 2048, "c1": 2048, "c2": 2048, "c3": 4096, "c4": 7168}
+
+
+def run_qkv_op(args, rank, world, dist):
+    """One decode token's q/k/v projection + rotary + KV store on one layer's
+    shape (B=1): the fused kernel against the unfused sequence (three cuBLAS
+    projections, then the RoPE + KV-store kernel), both replayed from CUDA
+    graphs with L2 flushed between launches. Bytes counted: the three weight
+    matrices (the rest is a few KB)."""
+    import torch
+    from sabrecoder_b200 import kernels as K
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    Hq, Hkv, L, _ = DECODE_SHAPES[args.workload]
+    hidden, D, T = HIDDEN[args.workload], 128, L + 64
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.randn(1, hidden, device=dev, generator=g, dtype=torch.bfloat16)
+    w = [torch.randn(h * D, hidden, device=dev, generator=g, dtype=torch.bfloat16) / hidden ** 0.5
+         for h in (Hq, Hkv, Hkv)]
+    cos = torch.randn(1, D, device=dev, generator=g, dtype=torch.bfloat16)
+    sin = torch.randn(1, D, device=dev, generator=g, dtype=torch.bfloat16)
+    kc = torch.zeros(1, Hkv, T, D, device=dev, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    q = torch.empty(1, Hq, D, device=dev, dtype=torch.bfloat16)
+    pos = L
+
+    def fused():
+        K.qkv_rope_decode(x, *w, cos, sin, q, kc, vc, pos)
+
+    def unfused():
+        qq = torch.nn.functional.linear(x, w[0]).view(1, 1, Hq, D)
+        kk = torch.nn.functional.linear(x, w[1]).view(1, 1, Hkv, D)
+        vv = torch.nn.functional.linear(x, w[2]).view(1, 1, Hkv, D)
+        K.rope_qkv(qq, kk, vv, cos.view(1, 1, D), sin.view(1, 1, D), kc, vc, pos0=pos)
+
+    flush = L2Flush(dev)
+    times = {}
+    for name, fn in (("fused", fused), ("unfused", unfused)):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(args.steps):
+            flush()
+            s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+            s.record()
+            graph.replay()
+            e.record()
+            torch.cuda.synchronize()
+            tot += s.elapsed_time(e)
+        times[name] = tot / args.steps
+        del graph
+    nbytes = (Hq + 2 * Hkv) * D * hidden * 2
+    gbs = nbytes / times["fused"] / 1e6
+    _, _, hbm, which = measured_peaks()
+    if rank == 0:
+        print(json.dumps({"metric": "decode q/k/v projection + rotary + KV store GB/s (single op)", "value": gbs,
+                          "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": times["fused"], "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                          "config": {"workload": f"{args.workload} decode q/k/v: B=1 hidden={hidden} Hq={Hq} "
+                                                 f"Hkv={Hkv}", "l2": L2Flush.NOTE,
+                                     "unfused_ms": times["unfused"]},
+                          "roofline": {"kernel": "sabre qkv_rope_decode_kernel", "bound": "hbm", "achieved": gbs,
+                                       "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                                       "peak_kind": f"{which} HBM copy bandwidth", "bytes_per_launch": nbytes,
+                                       "ms_per_launch": times["fused"], "traffic": None}}))
 
 
 def run_decode_op(args, rank, world, dist):

@@ -150,6 +150,31 @@ int sabre_rope_qkv(const void* q, const void* k, const void* v, const void* cos,
                    int dtype, void* stream);
 
 /* ------------------------------------------------------------------------
+ * (1c) Decode-step q/k/v projection + rotary embedding + KV store.
+ *
+ * Replaces, for one new token per sequence, the reference wrapper's
+ * q_proj/k_proj/v_proj, apply_rotary_pos_emb and KV-cache update
+ * (methods/sabrecoder/sabrecoder_llama_triton.py:288-299) with one kernel:
+ * y = W x for the three bias-free projections (fp32 sums, each output
+ * rounded to the storage dtype), then q_out = rope(y_q),
+ * k_out[pos0] = rope(y_k), v_out[pos0] = y_v with rope as in (1b).
+ *
+ * x        : [B, hidden] row stride x_stride (16-byte aligned)
+ * wq       : [heads_q*D, hidden], wk / wv: [heads_kv*D, hidden], row-major and
+ *            contiguous (16-byte aligned)
+ * cos, sin : [B, D] row stride cos_stride (the new token's position embeddings)
+ * q_out    : [B, heads_q, D] strides {b, h}
+ * k_out, v_out : [B, heads_kv, T, D] strides {b, h, t}; row pos0 is written
+ * batch <= 8, batch * hidden * 2 <= 160 KiB, hidden a multiple of 8,
+ * head_dim 128, d-stride 1 everywhere.
+ * ---------------------------------------------------------------------- */
+int sabre_qkv_rope_decode(const void* x, const void* wq, const void* wk, const void* wv, const void* cos,
+                          const void* sin, void* q_out, void* k_out, void* v_out, int batch, int hidden,
+                          int heads_q, int heads_kv, int head_dim, int pos0, int64_t x_stride,
+                          int64_t cos_stride, const int64_t* q_out_strides, const int64_t* k_out_strides,
+                          const int64_t* v_out_strides, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * (3) Block-mask construction from token-level structure.
  *
  * Replaces `StructureAwareMaskBuilder._build_block_mask_from_chunks`

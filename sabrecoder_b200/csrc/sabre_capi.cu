@@ -13,6 +13,7 @@
 #include "decode_bsa.cu"
 #include "block_mask.cu"
 #include "rope_cache.cu"
+#include "qkv_decode.cu"
 #include "topk.cu"
 #include "similarity.cu"
 #include "token_mask.cu"

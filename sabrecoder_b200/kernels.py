@@ -162,6 +162,38 @@ def rope_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tenso
     return q_out, qp, kp
 
 
+def qkv_rope_decode(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, cos: torch.Tensor,
+                    sin: torch.Tensor, q_out: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor,
+                    pos0: int) -> torch.Tensor:
+    """One decode token per sequence: ``q_out = rope(x @ wq.T)``, row ``pos0``
+    of ``k_out`` / ``v_out`` = ``rope(x @ wk.T)`` / ``x @ wv.T`` (bias-free
+    projections, each output rounded to the storage dtype, rope as in
+    ``rope_qkv``).
+
+    x: ``[B, hidden]``; w*: ``[H* * 128, hidden]`` contiguous; cos, sin:
+    ``[B, 128]``; q_out: ``[B, Hq, 128]``; k_out, v_out: ``[B, Hkv, T, 128]``.
+    Returns q_out."""
+    _need_cuda(x=x, wq=wq, wk=wk, wv=wv, cos=cos, sin=sin, q_out=q_out, k_out=k_out, v_out=v_out)
+    ts = (x, wq, wk, wv, cos, sin, q_out, k_out, v_out)
+    if x.dtype not in DTYPE_CODE or any(t.dtype != x.dtype for t in ts):
+        raise SabreError("qkv_rope_decode: all tensors must share dtype bf16 or f16")
+    if not (wq.is_contiguous() and wk.is_contiguous() and wv.is_contiguous()):
+        raise SabreError("qkv_rope_decode: weights must be contiguous")
+    if x.stride(-1) != 1 or cos.stride(-1) != 1 or sin.stride() != cos.stride():
+        raise SabreError("qkv_rope_decode: x, cos and sin need unit last stride (cos and sin alike)")
+    B, hidden = x.shape
+    D = q_out.shape[-1]
+    Hq, Hkv = wq.shape[0] // D, wk.shape[0] // D
+    st = lib().sabre_qkv_rope_decode(
+        x.data_ptr(), wq.data_ptr(), wk.data_ptr(), wv.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+        q_out.data_ptr(), k_out.data_ptr(), v_out.data_ptr(), B, hidden, Hq, Hkv, D, int(pos0), x.stride(0),
+        cos.stride(0), i64((q_out.stride(0), q_out.stride(1))), i64(k_out.stride()[:3]), i64(v_out.stride()[:3]),
+        DTYPE_CODE[x.dtype], _stream(x))
+    check(st, "sabre_qkv_rope_decode")
+    LAUNCHES[0] += 1
+    return q_out
+
+
 # ---------------------------------------------------------------------------
 # (2) decode
 # ---------------------------------------------------------------------------

@@ -223,6 +223,28 @@ class StructureAwareAttentionWrapper(nn.Module):
         self.o_proj = original_attn.o_proj
         self._prompt_len = 0
 
+    def _fused_decode_ok(self, hidden_states: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> bool:
+        """Whether a one-token step can use the fused projection + rotary +
+        KV-store kernel: plain bias-free projections with contiguous weights
+        of the activations' dtype, and shapes the kernel takes."""
+        projs = (self.q_proj, self.k_proj, self.v_proj)
+        if any(not isinstance(m, nn.Linear) or m.bias is not None for m in projs):
+            return False
+        dt = hidden_states.dtype
+        if dt not in (torch.bfloat16, torch.float16) or not hidden_states.is_cuda:
+            return False
+        if any(m.weight.dtype != dt or not m.weight.is_contiguous() or m.weight.device != hidden_states.device
+               for m in projs):
+            return False
+        B, _, hidden = hidden_states.shape
+        if B > 8 or hidden % 8 or B * hidden * 2 > 160 * 1024 or self.head_dim != 128:
+            return False
+        if not hidden_states.is_contiguous() or cos.dtype != dt or sin.dtype != dt:
+            return False
+        if cos.numel() != B * self.head_dim or sin.shape != cos.shape:
+            return False
+        return hidden_states.data_ptr() % 16 == 0 and all(m.weight.data_ptr() % 16 == 0 for m in projs)
+
     def forward(self, hidden_states: torch.Tensor, position_embeddings: Tuple[torch.Tensor, torch.Tensor] = None,
                 attention_mask: Optional[torch.Tensor] = None, past_key_value=None,
                 cache_position: Optional[torch.LongTensor] = None, past_key_values=None, **kwargs):
@@ -230,25 +252,43 @@ class StructureAwareAttentionWrapper(nn.Module):
         cache = past_key_values if past_key_values is not None else past_key_value
         B, L = hidden_states.shape[:2]
         D = self.head_dim
-        q = self.q_proj(hidden_states).view(B, L, -1, D)
-        k = self.k_proj(hidden_states).view(B, L, -1, D)
-        v = self.v_proj(hidden_states).view(B, L, -1, D)
         cos, sin = position_embeddings
-        Hq, Hkv = q.shape[2], k.shape[2]
-        # One kernel rotates q in place and writes rotated K and V rows into
-        # [B, Hkv, T, D] storage (the cache's own buffers when it is a
-        # SabreKVCache); a fresh prefill also gets the per-block pooled q/k
-        # the top-k extension needs.
-        pool_block = self.block_size if (L > 1 and self.sparse_attn.topk_blocks > 0) else 0
+        qp = kp = None
+        if L == 1 and self._fused_decode_ok(hidden_states, cos, sin):
+            # One token per sequence: one kernel does the three projections,
+            # the rotation and the K/V store.
+            Hq = self.q_proj.weight.shape[0] // D
+            Hkv = self.k_proj.weight.shape[0] // D
+            w = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
+            q = torch.empty(B, 1, Hq, D, dtype=hidden_states.dtype, device=hidden_states.device)
+
+            def store(k_out, v_out, pos):
+                K.qkv_rope_decode(hidden_states.view(B, -1), *w, cos.reshape(B, D), sin.reshape(B, D),
+                                  q.view(B, Hq, D), k_out, v_out, pos)
+        else:
+            q = self.q_proj(hidden_states).view(B, L, -1, D)
+            k = self.k_proj(hidden_states).view(B, L, -1, D)
+            v = self.v_proj(hidden_states).view(B, L, -1, D)
+            Hq, Hkv = q.shape[2], k.shape[2]
+            # One kernel rotates q in place and writes rotated K and V rows;
+            # a fresh prefill also gets the per-block pooled q/k the top-k
+            # extension needs.
+            pool_block = self.block_size if (L > 1 and self.sparse_attn.topk_blocks > 0) else 0
+
+            def store(k_out, v_out, pos):
+                nonlocal qp, kp
+                _, qp, kp = K.rope_qkv(q, k, v, cos, sin, k_out, v_out, pos0=pos,
+                                       pool_block=pool_block if pos == 0 else 0)
+        # K and V rows go into [B, Hkv, T, D] storage: the cache's own buffers
+        # when it is a SabreKVCache, else new rows handed to the cache's update.
         if isinstance(cache, SabreKVCache):
             kbuf, vbuf, pos0 = cache.slots(self.layer_idx, L)
-            _, qp, kp = K.rope_qkv(q, k, v, cos, sin, kbuf, vbuf, pos0=pos0,
-                                   pool_block=pool_block if pos0 == 0 else 0)
+            store(kbuf, vbuf, pos0)
             kh, vh = cache.advance(self.layer_idx, L)
         else:
             kn = torch.empty(B, Hkv, L, D, dtype=q.dtype, device=q.device)
             vn = torch.empty_like(kn)
-            _, qp, kp = K.rope_qkv(q, k, v, cos, sin, kn, vn, pool_block=pool_block)
+            store(kn, vn, 0)
             kh, vh = kn, vn
             if cache is not None:
                 kh, vh = cache.update(kn, vn, self.layer_idx,

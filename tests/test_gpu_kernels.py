@@ -335,6 +335,41 @@ def test_decode_strided_cache_vs_oracle(K, block, row_pad, Hq):
     _close(out, ref)
 
 
+@pytest.mark.parametrize("B,hidden,Hq,Hkv,dtype", [(1, 2048, 16, 16, torch.bfloat16), (3, 1024, 8, 2, torch.bfloat16),
+                                                  (2, 1792, 14, 2, torch.float16)])
+def test_qkv_rope_decode_vs_unfused(K, B, hidden, Hq, Hkv, dtype):
+    """The fused decode projection + rotary + KV store against the unfused
+    computation (cuBLAS projection rounded to the dtype, then transformers'
+    apply_rotary_pos_emb); they differ only by the projection's summation
+    order, so outputs agree within two ulps. Other cache rows stay untouched."""
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+    gen = torch.Generator().manual_seed(hidden + Hq)
+    D, T, pos = 128, 40, 29
+    dev = torch.device("cuda")
+    x = torch.randn(B, hidden, generator=gen).to(dtype).to(dev)
+    w = [(torch.randn(h * D, hidden, generator=gen) / hidden ** 0.5).to(dtype).to(dev) for h in (Hq, Hkv, Hkv)]
+    ang = torch.rand(B, D // 2, generator=gen) * 6.0
+    emb = torch.cat([ang, ang], dim=-1)
+    cos, sin = emb.cos().to(dtype).to(dev), emb.sin().to(dtype).to(dev)
+    sentinel = torch.full((B, Hkv, T, D), 7.0, dtype=dtype, device=dev)
+    kc, vc = sentinel.clone(), sentinel.clone()
+    q = torch.empty(B, Hq, D, dtype=dtype, device=dev)
+    K.qkv_rope_decode(x, w[0], w[1], w[2], cos, sin, q, kc, vc, pos)
+    torch.cuda.synchronize()
+    yq = torch.nn.functional.linear(x, w[0]).view(B, 1, Hq, D).transpose(1, 2)
+    yk = torch.nn.functional.linear(x, w[1]).view(B, 1, Hkv, D).transpose(1, 2)
+    yv = torch.nn.functional.linear(x, w[2]).view(B, Hkv, D)
+    rq, rk = apply_rotary_pos_emb(yq, yk, cos.unsqueeze(1), sin.unsqueeze(1))
+    tol = dict(rtol=2 ** -6, atol=2 ** -6)
+    torch.testing.assert_close(q.float(), rq[:, :, 0].float(), **tol)
+    torch.testing.assert_close(kc[:, :, pos].float(), rk[:, :, 0].float(), **tol)
+    torch.testing.assert_close(vc[:, :, pos].float(), yv.float(), **tol)
+    others = torch.ones(T, dtype=torch.bool)
+    others[pos] = False
+    assert torch.equal(kc[:, :, others], sentinel[:, :, others])
+    assert torch.equal(vc[:, :, others], sentinel[:, :, others])
+
+
 def test_no_device_timeouts_recorded(K):
     assert K.device_status(clear=True) == 0
 
