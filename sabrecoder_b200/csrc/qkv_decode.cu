@@ -62,7 +62,7 @@ __device__ __forceinline__ void unpack8q(const uint4& u, float (&f)[8]) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads) qkv_rope_decode_kernel(const Params p) {
+__global__ void __launch_bounds__(kThreads, 2) qkv_rope_decode_kernel(const Params p) {
   extern __shared__ uint4 sx[];  // [B][hidden / 8]
   __shared__ float sy[kMaxBatch][2 * kPairs];
   const int tid = threadIdx.x;
@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kThreads) qkv_rope_decode_kernel(const Params 
   for (int u = 0; u < 4; ++u)
 #pragma unroll
     for (int b = 0; b < kMaxBatch; ++b) acc[u][b] = 0.f;
-#pragma unroll 2
+#pragma unroll 4
   for (int c = lane; c < nch; c += 32) {
     float wf[4][8];
 #pragma unroll
