@@ -4,7 +4,7 @@
 // Replaces, for one new token per sequence, the reference wrapper's
 // q_proj/k_proj/v_proj calls, apply_rotary_pos_emb and the KV-cache update
 // (methods/sabrecoder/sabrecoder_llama_triton.py:288-299): three matrix-vector
-// products whose weights (2.7 GB of HBM traffic per token at 33B) dominate,
+// products whose weights (132 MB per layer, 8.2 GB per token at 33B) dominate,
 // followed by a rotation and a cache write that separately cost a launch and
 // a round trip each. Here every CTA streams 32 weight rows of one head with
 // coalesced 16-byte loads (a warp covers 512 contiguous bytes of a row per
