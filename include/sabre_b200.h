@@ -164,13 +164,13 @@ int sabre_rope_qkv(const void* q, const void* k, const void* v, const void* cos,
  *            contiguous (16-byte aligned)
  * cos, sin : [B, D] row stride cos_stride (the new token's position embeddings)
  * q_out    : [B, heads_q, D] strides {b, h}
- * k_out, v_out : [B, heads_kv, T, D] strides {b, h, t}; row pos0 is written
+ * k_out, v_out : [B, heads_kv, T, D] strides {b, h, t}, T = max_seq; row pos0 (< T) is written
  * batch <= 8, batch * hidden * 2 <= 160 KiB, hidden a multiple of 8,
  * head_dim 128, d-stride 1 everywhere.
  * ---------------------------------------------------------------------- */
 int sabre_qkv_rope_decode(const void* x, const void* wq, const void* wk, const void* wv, const void* cos,
                           const void* sin, void* q_out, void* k_out, void* v_out, int batch, int hidden,
-                          int heads_q, int heads_kv, int head_dim, int pos0, int64_t x_stride,
+                          int heads_q, int heads_kv, int head_dim, int pos0, int max_seq, int64_t x_stride,
                           int64_t cos_stride, const int64_t* q_out_strides, const int64_t* k_out_strides,
                           const int64_t* v_out_strides, int dtype, void* stream);
 

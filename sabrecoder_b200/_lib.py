@@ -34,7 +34,7 @@ SIGNATURES = {
     "sabre_rope_qkv": (c_int, [P, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                I64P, I64P, I64P, I64P, I64P, I64P, I64P, c_int, P]),
     "sabre_qkv_rope_decode": (c_int, [P, P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
-                                      c_int64, c_int64, I64P, I64P, I64P, c_int, P]),
+                                      c_int, c_int64, c_int64, I64P, I64P, I64P, c_int, P]),
     "sabre_block_mask_workspace_size": (c_size_t, [c_int, c_int]),
     "sabre_build_block_mask": (c_int, [P, P, P, c_int, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                        P, P, P, c_size_t, P]),

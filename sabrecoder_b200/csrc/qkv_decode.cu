@@ -174,15 +174,18 @@ extern "C" {
 
 int sabre_qkv_rope_decode(const void* x, const void* wq, const void* wk, const void* wv, const void* cos,
                           const void* sin, void* q_out, void* k_out, void* v_out, int batch, int hidden,
-                          int heads_q, int heads_kv, int head_dim, int pos0, int64_t x_stride,
+                          int heads_q, int heads_kv, int head_dim, int pos0, int max_seq, int64_t x_stride,
                           int64_t cos_stride, const int64_t* q_out_strides, const int64_t* k_out_strides,
                           const int64_t* v_out_strides, int dtype, void* stream) {
   using namespace sabre::qkvd;
   if (!x || !wq || !wk || !wv || !cos || !sin || !q_out || !k_out || !v_out || !q_out_strides || !k_out_strides ||
       !v_out_strides)
     return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_qkv_rope_decode: null pointer argument");
-  if (batch <= 0 || hidden <= 0 || heads_q <= 0 || heads_kv <= 0 || pos0 < 0)
+  if (batch <= 0 || hidden <= 0 || heads_q <= 0 || heads_kv <= 0 || max_seq <= 0)
     return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_qkv_rope_decode: sizes must be positive");
+  if (pos0 < 0 || pos0 >= max_seq)
+    return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_qkv_rope_decode: position %d outside the cache's %d rows", pos0,
+                      max_seq);
   if (head_dim != kD)
     return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_qkv_rope_decode: head_dim %d (only 128)", head_dim);
   if (dtype != SABRE_BF16 && dtype != SABRE_F16)

@@ -184,9 +184,15 @@ def qkv_rope_decode(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: tor
     B, hidden = x.shape
     D = q_out.shape[-1]
     Hq, Hkv = wq.shape[0] // D, wk.shape[0] // D
+    T = k_out.shape[2] if k_out.dim() == 4 else 0
+    if (wq.shape != (Hq * D, hidden) or wk.shape != (Hkv * D, hidden) or wv.shape != wk.shape
+            or tuple(cos.shape) != (B, D) or tuple(q_out.shape) != (B, Hq, D)
+            or k_out.dim() != 4 or tuple(k_out.shape) != (B, Hkv, T, D) or v_out.shape != k_out.shape):
+        raise SabreError("qkv_rope_decode: shapes do not match x [B, hidden], w [H*D, hidden], cos [B, D], "
+                         "q_out [B, Hq, D], k_out/v_out [B, Hkv, T, D]")
     st = lib().sabre_qkv_rope_decode(
         x.data_ptr(), wq.data_ptr(), wk.data_ptr(), wv.data_ptr(), cos.data_ptr(), sin.data_ptr(),
-        q_out.data_ptr(), k_out.data_ptr(), v_out.data_ptr(), B, hidden, Hq, Hkv, D, int(pos0), x.stride(0),
+        q_out.data_ptr(), k_out.data_ptr(), v_out.data_ptr(), B, hidden, Hq, Hkv, D, int(pos0), T, x.stride(0),
         cos.stride(0), i64((q_out.stride(0), q_out.stride(1))), i64(k_out.stride()[:3]), i64(v_out.stride()[:3]),
         DTYPE_CODE[x.dtype], _stream(x))
     check(st, "sabre_qkv_rope_decode")

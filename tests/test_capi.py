@@ -66,6 +66,19 @@ def test_decode_and_mask_reject_bad_arguments():
     assert r == -5
 
 
+def test_qkv_rope_decode_rejects_positions_outside_the_cache():
+    L = _lib.lib()
+    st = _lib.i64([1, 1, 1])
+    args = lambda pos, t: (16, 16, 16, 16, 16, 16, 16, 16, 16, 1, 2048, 16, 16, 128, pos, t, 2048, 128, st, st, st,
+                           0, None)
+    assert L.sabre_qkv_rope_decode(*args(64, 64)) == -1 and b"outside" in L.sabre_last_error()
+    assert L.sabre_qkv_rope_decode(*args(-1, 64)) == -1
+    assert L.sabre_qkv_rope_decode(*args(0, 0)) == -1
+    r = L.sabre_qkv_rope_decode(16, 16, 16, 16, 16, 16, 16, 16, 16, 9, 2048, 16, 16, 128, 0, 8, 2048, 128, st, st,
+                                st, 0, None)
+    assert r == -2 and b"batch" in L.sabre_last_error()
+
+
 def test_kernel_calls_fail_loudly_without_cuda_tensors():
     import torch
     from sabrecoder_b200 import kernels
