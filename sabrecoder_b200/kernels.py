@@ -131,6 +131,9 @@ def rope_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tenso
     q_out defaults to q (rotated in place). With ``pool_block > 0`` also
     returns fp32 per-block means of the rotated q and k
     (``[B, Hq, nb, D]``, ``[B, Hkv, nb, D]``). Returns ``(q_out, q_pool, k_pool)``."""
+    if k_out.dim() != 4 or v_out.shape != k_out.shape or pos0 < 0 or pos0 + q.shape[1] > k_out.shape[2]:
+        raise SabreError(f"rope_qkv: rows {pos0}..{pos0 + q.shape[1] - 1} do not fit k_out/v_out of shape "
+                         f"{tuple(k_out.shape)} (need [B, Hkv, T, D] with pos0 + L <= T)")
     _need_cuda(q=q, k=k, v=v, cos=cos, sin=sin, k_out=k_out, v_out=v_out)
     if q.dtype not in DTYPE_CODE or any(t.dtype != q.dtype for t in (k, v, cos, sin, k_out, v_out)):
         raise SabreError("rope_qkv: q/k/v/cos/sin/k_out/v_out must share dtype bf16 or f16")

@@ -79,6 +79,16 @@ def test_qkv_rope_decode_rejects_positions_outside_the_cache():
     assert r == -2 and b"batch" in L.sabre_last_error()
 
 
+def test_rope_qkv_rejects_rows_past_the_cache():
+    import torch
+    from sabrecoder_b200 import kernels
+    q = torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)
+    kv = torch.zeros(1, 2, 8, 128, dtype=torch.bfloat16)
+    cs = torch.zeros(1, 4, 128, dtype=torch.bfloat16)
+    with pytest.raises(_lib.SabreError, match="do not fit"):
+        kernels.rope_qkv(q, q, q, cs, cs, kv, kv, pos0=5)
+
+
 def test_kernel_calls_fail_loudly_without_cuda_tensors():
     import torch
     from sabrecoder_b200 import kernels
