@@ -39,6 +39,7 @@ to a syntax error may differ from tree-sitter's.
 from __future__ import annotations
 
 import ast
+from collections import deque
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -111,14 +112,47 @@ def _neutralised(lines: List[str], max_fixes: int) -> Optional[ast.Module]:
     return None
 
 
+# The segmenter and the analyser parse the same prompt one after the other;
+# the last parse is kept (the trees are only read).
+_PARSE_CACHE: Dict[Tuple[str, int, int], Tuple[Optional[ast.Module], int]] = {}
+
+
 def _parse(code: str, max_trim_lines: int, max_fixes: int = 64) -> Tuple[Optional[ast.Module], int]:
     """(module, number of trailing lines dropped to make it parse)."""
+    key = (code, max_trim_lines, max_fixes)
+    hit = _PARSE_CACHE.get(key)
+    if hit is not None:
+        return hit
+    result: Tuple[Optional[ast.Module], int] = (None, 0)
     lines = code.split("\n")
     for drop in range(0, min(max_trim_lines, len(lines) - 1) + 1):
         tree = _neutralised(lines[: len(lines) - drop], max_fixes if drop == 0 else 0)
         if tree is not None:
-            return tree, drop
-    return None, 0
+            result = (tree, drop)
+            break
+    _PARSE_CACHE.clear()
+    _PARSE_CACHE[key] = result
+    return result
+
+
+def _calls(tree: ast.AST) -> List[ast.Call]:
+    """The Call nodes of a tree in ``ast.walk`` order (breadth first, fields
+    in declaration order), without its per-node generators."""
+    AST, Call = ast.AST, ast.Call
+    out: List[ast.Call] = []
+    todo = deque([tree])
+    pop, push, extend = todo.popleft, todo.append, todo.extend
+    while todo:
+        node = pop()
+        if node.__class__ is Call:
+            out.append(node)
+        for name in node._fields:
+            v = getattr(node, name, None)
+            if v.__class__ is list:
+                extend([x for x in v if isinstance(x, AST)])
+            elif isinstance(v, AST):
+                push(v)
+    return out
 
 
 class PythonSegmenter:
@@ -275,9 +309,7 @@ class PythonReferenceAnalyzer:
         self.references = []
         if tree is None:
             return self.references
-        for node in ast.walk(tree):
-            if not isinstance(node, ast.Call):
-                continue
+        for node in _calls(tree):
             line = node.lineno
             source = self.chunk_by_line.get(line)
             if source is None:
