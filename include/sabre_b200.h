@@ -115,7 +115,10 @@ int sabre_decode_bsa(const void* q, const void* k_cache, const void* v_cache, vo
  * SABRE_ERR_UNSUPPORTED. All calls share that array, so calls that overlap
  * on the GPU race. The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current; make it before
- * any stream capture.
+ * any stream capture. The address is kept for the life of the process: after
+ * a cudaDeviceReset the module is loaded again and the array may move, so a
+ * process that resets a device must reload this library before calling this
+ * entry point again.
  * ---------------------------------------------------------------------- */
 int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_cache, void* o,
                              const int32_t* block_indices, const int32_t* block_counts, const int32_t* seq_lens,
@@ -136,7 +139,9 @@ int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_c
  * q, k, v  : [B, L, H*, D] strides {b, l, h} (d-stride 1)
  * cos, sin : [B, L, D] strides {b, l} (the model's position embeddings)
  * q_out    : [B, L, Hq, D] strides {b, l, h} (may alias q)
- * k_out, v_out : [B, Hkv, T, D] strides {b, h, t}; rows pos0 .. pos0+L-1
+ * k_out, v_out : [B, Hkv, T, D] strides {b, h, t}, T = max_seq; rows
+ *            pos0 .. pos0+L-1 are written (pos0 >= 0 and pos0 + L <= T, else
+ *            SABRE_ERR_INVALID_ARG before launch)
  * q_pool, k_pool (optional, fp32, contiguous [B, Hq|Hkv, ceil(L/pool_block), D]):
  *            per-block means of the rotated rows (rows summed first to
  *            last, then divided by the row count); require pos0 == 0.
@@ -144,7 +149,7 @@ int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_c
  * ---------------------------------------------------------------------- */
 int sabre_rope_qkv(const void* q, const void* k, const void* v, const void* cos, const void* sin, void* q_out,
                    void* k_out, void* v_out, float* q_pool, float* k_pool, int batch, int seq_len, int heads_q,
-                   int heads_kv, int head_dim, int pool_block, int pos0, const int64_t* q_strides,
+                   int heads_kv, int head_dim, int pool_block, int pos0, int max_seq, const int64_t* q_strides,
                    const int64_t* k_strides, const int64_t* v_strides, const int64_t* cos_strides,
                    const int64_t* q_out_strides, const int64_t* k_out_strides, const int64_t* v_out_strides,
                    int dtype, void* stream);

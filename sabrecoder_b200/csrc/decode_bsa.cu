@@ -677,8 +677,12 @@ int sabre_decode_bsa(const void* q, const void* k_cache, const void* v_cache, vo
 //
 // The array is kNoAllocScratchFloats floats (2 MiB); every GPU that loads the
 // library holds it until the process exits. One decode call needs
-// batch * heads_q * splits * (head_dim + 2) floats; the entry point lowers the
-// split count to fit and rejects shapes that do not fit even with one split.
+// batch * heads_q * splits * (head_dim + 2) floats. choose_splits picks
+// either one split or a count with splits * batch * heads_kv <= kTargetCtas;
+// with at most 8 query heads per KV head the latter needs at most
+// kTargetCtas * 8 * (head_dim + 2) floats, which the array holds
+// (static_assert below). So the only shapes turned away are those whose
+// batch * heads_q * (head_dim + 2) floats do not fit even with one split.
 // All calls share the array: calls whose kernels overlap on the GPU (on
 // different streams, or on other host threads) race on it. Each call's split
 // kernel writes every partial it later reads, so nothing needs clearing
@@ -696,6 +700,9 @@ namespace decode {
 
 constexpr size_t kNoAllocScratchFloats = 512u * 1024u;  // 2 MiB
 constexpr int kNoAllocMaxDevices = 64;
+
+static_assert(static_cast<size_t>(kTargetCtas) * 8 * (kD + 2) <= kNoAllocScratchFloats,
+              "the split partials of every accepted decode shape must fit the no-alloc scratch");
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 static float* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {nullptr};
@@ -753,10 +760,10 @@ int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_c
     if ((ss[i] * 2) % 16 != 0)
       return sabre_fail(SABRE_ERR_ALIGNMENT, "sabre_decode_bsa_noalloc: q/k/v strides must be 16-byte multiples");
 
-  // Fit the split partials into the fixed array.
+  // The split partials must fit the fixed array: a shape that fits with one
+  // split fits with the count choose_splits picks (static_assert above).
   const size_t per_split = static_cast<size_t>(batch) * heads_q * (static_cast<size_t>(kD) + 2);
-  const size_t max_splits_fit = kNoAllocScratchFloats / per_split;
-  if (max_splits_fit < 1)
+  if (per_split > kNoAllocScratchFloats)
     return sabre_fail(SABRE_ERR_UNSUPPORTED,
                       "sabre_decode_bsa_noalloc: batch*heads_q = %lld needs %zu floats of scratch per split; the "
                       "built-in scratch holds %zu floats (2 MiB); use sabre_decode_bsa with a workspace",
@@ -794,9 +801,7 @@ int sabre_decode_bsa_noalloc(const void* q, const void* k_cache, const void* v_c
   p.Tmax = max_seq;
   p.block = block_size;
   p.max_active = max_active;
-  int splits = choose_splits(batch, heads_kv, max_active);
-  if (static_cast<size_t>(splits) > max_splits_fit) splits = static_cast<int>(max_splits_fit);
-  p.splits = splits;
+  p.splits = choose_splits(batch, heads_kv, max_active);
   p.bps = (max_active + p.splits - 1) / p.splits;
   const size_t nslots = static_cast<size_t>(batch) * heads_q * p.splits;
   p.part_acc = scratch;

@@ -213,7 +213,7 @@ extern "C" {
 
 int sabre_rope_qkv(const void* q, const void* k, const void* v, const void* cos, const void* sin, void* q_out,
                    void* k_out, void* v_out, float* q_pool, float* k_pool, int batch, int seq_len, int heads_q,
-                   int heads_kv, int head_dim, int pool_block, int pos0, const int64_t* q_strides,
+                   int heads_kv, int head_dim, int pool_block, int pos0, int max_seq, const int64_t* q_strides,
                    const int64_t* k_strides, const int64_t* v_strides, const int64_t* cos_strides,
                    const int64_t* q_out_strides, const int64_t* k_out_strides, const int64_t* v_out_strides,
                    int dtype, void* stream) {
@@ -223,6 +223,10 @@ int sabre_rope_qkv(const void* q, const void* k, const void* v, const void* cos,
     return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_rope_qkv: null pointer argument");
   if (batch <= 0 || seq_len <= 0 || heads_q <= 0 || heads_kv <= 0 || pos0 < 0)
     return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_rope_qkv: sizes must be positive");
+  if (static_cast<long long>(pos0) + seq_len > static_cast<long long>(max_seq))
+    return sabre_fail(SABRE_ERR_INVALID_ARG,
+                      "sabre_rope_qkv: rows %d..%lld lie outside the cache of %d rows (k_out/v_out)", pos0,
+                      static_cast<long long>(pos0) + seq_len - 1, max_seq);
   if (head_dim != kD) return sabre_fail(SABRE_ERR_UNSUPPORTED, "sabre_rope_qkv: head_dim %d (only 128)", head_dim);
   if (dtype != SABRE_BF16 && dtype != SABRE_F16)
     return sabre_fail(SABRE_ERR_INVALID_ARG, "sabre_rope_qkv: dtype %d", dtype);

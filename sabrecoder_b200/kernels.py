@@ -134,11 +134,20 @@ def rope_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tenso
     if k_out.dim() != 4 or v_out.shape != k_out.shape or pos0 < 0 or pos0 + q.shape[1] > k_out.shape[2]:
         raise SabreError(f"rope_qkv: rows {pos0}..{pos0 + q.shape[1] - 1} do not fit k_out/v_out of shape "
                          f"{tuple(k_out.shape)} (need [B, Hkv, T, D] with pos0 + L <= T)")
+    if q.dim() != 4 or k.dim() != 4 or v.shape != k.shape or k.shape[:2] != q.shape[:2]:
+        raise SabreError(f"rope_qkv: q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} must be "
+                         f"[B, L, H*, D] with one B and L")
+    B, L, Hq, D = q.shape
+    Hkv = k.shape[2]
+    if tuple(k_out.shape[:2]) != (B, Hkv) or k_out.shape[3] != D:
+        raise SabreError(f"rope_qkv: k_out/v_out {tuple(k_out.shape)} do not match [B={B}, Hkv={Hkv}, T, D={D}]")
+    if cos.dim() not in (2, 3) or sin.shape != cos.shape or cos.shape[-1] != D or cos.shape[-2] < L or (
+            cos.dim() == 3 and cos.shape[0] != B):
+        raise SabreError(f"rope_qkv: cos/sin {tuple(cos.shape)} must be [B, >= L, D] or [>= L, D] "
+                         f"(B={B}, L={L}, D={D})")
     _need_cuda(q=q, k=k, v=v, cos=cos, sin=sin, k_out=k_out, v_out=v_out)
     if q.dtype not in DTYPE_CODE or any(t.dtype != q.dtype for t in (k, v, cos, sin, k_out, v_out)):
         raise SabreError("rope_qkv: q/k/v/cos/sin/k_out/v_out must share dtype bf16 or f16")
-    B, L, Hq, D = q.shape
-    Hkv = k.shape[2]
     if q_out is None:
         q_out = q
     if cos.dim() == 2:
@@ -158,7 +167,7 @@ def rope_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tenso
     st = lib().sabre_rope_qkv(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(), q_out.data_ptr(),
         k_out.data_ptr(), v_out.data_ptr(), _ptr(qp), _ptr(kp), B, L, Hq, Hkv, D, int(pool_block), int(pos0),
-        s3(q), s3(k), s3(v), i64((cos.stride(0), cos.stride(1))), s3(q_out), s3(k_out), s3(v_out),
+        int(k_out.shape[2]), s3(q), s3(k), s3(v), i64((cos.stride(0), cos.stride(1))), s3(q_out), s3(k_out), s3(v_out),
         DTYPE_CODE[q.dtype], _stream(q))
     check(st, "sabre_rope_qkv")
     LAUNCHES[0] += 1

@@ -39,6 +39,7 @@ to a syntax error may differ from tree-sitter's.
 from __future__ import annotations
 
 import ast
+import threading
 from collections import deque
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence, Tuple
@@ -112,17 +113,26 @@ def _neutralised(lines: List[str], max_fixes: int) -> Optional[ast.Module]:
     return None
 
 
-# The segmenter and the analyser parse the same prompt one after the other;
-# the last parse is kept (the trees are only read).
-_PARSE_CACHE: Dict[Tuple[str, int, int], Tuple[Optional[ast.Module], int]] = {}
+# The segmenter and the analyser parse the same prompt one after the other,
+# so each thread keeps its last parse (one entry per thread: a worker thread
+# never sees another thread's tree, and at most one prompt's text and tree per
+# thread stay alive after the call). Trees returned by _parse are shared by
+# both callers and must be treated as read-only.
+_PARSE_LOCAL = threading.local()
+
+
+def clear_parse_cache() -> None:
+    """Drop the calling thread's cached parse."""
+    _PARSE_LOCAL.entry = None
 
 
 def _parse(code: str, max_trim_lines: int, max_fixes: int = 64) -> Tuple[Optional[ast.Module], int]:
-    """(module, number of trailing lines dropped to make it parse)."""
+    """(module, number of trailing lines dropped to make it parse). The
+    module is cached for the calling thread and must not be modified."""
     key = (code, max_trim_lines, max_fixes)
-    hit = _PARSE_CACHE.get(key)
-    if hit is not None:
-        return hit
+    hit = getattr(_PARSE_LOCAL, "entry", None)
+    if hit is not None and hit[0] == key:
+        return hit[1]
     result: Tuple[Optional[ast.Module], int] = (None, 0)
     lines = code.split("\n")
     for drop in range(0, min(max_trim_lines, len(lines) - 1) + 1):
@@ -130,8 +140,7 @@ def _parse(code: str, max_trim_lines: int, max_fixes: int = 64) -> Tuple[Optiona
         if tree is not None:
             result = (tree, drop)
             break
-    _PARSE_CACHE.clear()
-    _PARSE_CACHE[key] = result
+    _PARSE_LOCAL.entry = (key, result)
     return result
 
 

@@ -1,10 +1,11 @@
 """Record golden vectors from the reference implementation.
 
-Runs only where the reference checkout is present (it is read from
-``/root/reference``); the GPU machines and the test suite use the committed
-``.npz`` files instead. Regenerate with::
+Runs only where the reference checkout is present; the GPU machines and the
+test suite use the committed ``.npz`` files instead. Regenerate with::
 
-    python tests/golden/gen_golden.py
+    python tests/golden/gen_golden.py --reference <checkout of SabreCoder>
+
+(or set ``SABRECODER_REF`` to the checkout).
 
 What is recorded (all from the reference's own code, unmodified):
 
@@ -45,7 +46,24 @@ import sys
 import types
 
 os.environ["TRITON_INTERPRET"] = "1"
-REF = "/root/reference"
+
+
+def _reference_root() -> str:
+    """The reference checkout: ``--reference PATH`` or ``$SABRECODER_REF``."""
+    for i, a in enumerate(sys.argv[1:], 1):
+        if a == "--reference" and i + 1 < len(sys.argv):
+            return sys.argv[i + 1]
+        if a.startswith("--reference="):
+            return a.split("=", 1)[1]
+    ref = os.environ.get("SABRECODER_REF")
+    if not ref:
+        sys.exit("gen_golden.py: give the reference checkout with --reference PATH or SABRECODER_REF")
+    return ref
+
+
+REF = _reference_root()
+if not os.path.isdir(os.path.join(REF, "methods", "sabrecoder")):
+    sys.exit(f"gen_golden.py: {REF} does not hold methods/sabrecoder")
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 
@@ -820,10 +838,18 @@ def main():
 
 
 if __name__ == "__main__":
-    # No argument: every fixture. Otherwise the named recorders only, e.g.
-    # "python tests/golden/gen_golden.py crossfile".
-    if len(sys.argv) > 1:
-        for _n in sys.argv[1:]:
+    # No recorder named: every fixture. Otherwise the named recorders only, e.g.
+    # "python tests/golden/gen_golden.py --reference PATH crossfile".
+    _names, _skip = [], False
+    for _a in sys.argv[1:]:
+        if _skip:
+            _skip = False
+        elif _a == "--reference":
+            _skip = True
+        elif not _a.startswith("--reference="):
+            _names.append(_a)
+    if _names:
+        for _n in _names:
             globals()[f"record_{_n}"]()
     else:
         main()

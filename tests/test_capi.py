@@ -89,6 +89,46 @@ def test_rope_qkv_rejects_rows_past_the_cache():
         kernels.rope_qkv(q, q, q, cs, cs, kv, kv, pos0=5)
 
 
+def test_rope_qkv_c_entry_checks_rows_against_the_cache():
+    """The C entry point itself rejects rows outside [0, max_seq) (callers
+    from other languages do not pass through the Python checks)."""
+    L = _lib.lib()
+    st = _lib.i64([1024, 1024, 128])
+
+    def call(pos0, seq_len, max_seq):
+        return L.sabre_rope_qkv(16, 16, 16, 16, 16, 16, 16, 16, None, None, 1, seq_len, 2, 2, 128, 0, pos0,
+                                max_seq, st, st, st, st, st, st, st, 0, None)
+
+    assert call(5, 4, 8) == -1 and b"outside the cache" in L.sabre_last_error()
+    assert call(0, 9, 8) == -1 and b"outside the cache" in L.sabre_last_error()
+    assert call(-1, 4, 8) == -1
+    assert call(2147483647, 4, 8) == -1  # pos0 + L overflows int32
+    assert call(0, 4, 0) == -1
+
+
+@pytest.mark.parametrize("what", ["cos_rows", "cos_batch", "kout_batch", "kout_heads", "k_len"])
+def test_rope_qkv_rejects_mismatched_shapes(what):
+    import torch
+    from sabrecoder_b200 import kernels
+    B, L, Hq, Hkv, D, T = 2, 4, 4, 2, 128, 8
+    q = torch.zeros(B, L, Hq, D, dtype=torch.bfloat16)
+    k = torch.zeros(B, L, Hkv, D, dtype=torch.bfloat16)
+    cs = torch.zeros(B, L, D, dtype=torch.bfloat16)
+    kv = torch.zeros(B, Hkv, T, D, dtype=torch.bfloat16)
+    if what == "cos_rows":
+        cs = torch.zeros(B, L - 1, D, dtype=torch.bfloat16)
+    elif what == "cos_batch":
+        cs = torch.zeros(B + 1, L, D, dtype=torch.bfloat16)
+    elif what == "kout_batch":
+        kv = torch.zeros(B - 1, Hkv, T, D, dtype=torch.bfloat16)
+    elif what == "kout_heads":
+        kv = torch.zeros(B, Hkv + 1, T, D, dtype=torch.bfloat16)
+    else:
+        k = torch.zeros(B, L + 1, Hkv, D, dtype=torch.bfloat16)
+    with pytest.raises(_lib.SabreError, match="rope_qkv"):
+        kernels.rope_qkv(q, k, k, cs, cs, kv, kv)
+
+
 def test_kernel_calls_fail_loudly_without_cuda_tensors():
     import torch
     from sabrecoder_b200 import kernels

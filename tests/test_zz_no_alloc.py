@@ -1,18 +1,22 @@
-"""The allocation-free decode entry point against the workspace one.
+"""The allocation-free decode entry point against the workspace one and the
+oracle.
 
 sabre_decode_bsa_noalloc serves callers that cannot give this library any
 device memory at decode time (a runtime that reserved all memory at start-up,
 a binding with no allocator of its own). Its split partials live in a fixed
 array inside the library, so this test calls it twice in a row with different
-inputs through the C ABI and checks each result against sabre_decode_bsa
-(same tolerance as the other attention tests): the second call must not see
-the first call's leftovers. The file is named to be collected last.
+inputs through the C ABI and checks each result against sabre_decode_bsa and
+the oracle's decode (same tolerance as the other attention tests): the second
+call must not see the first call's leftovers. The file is named to be
+collected last.
 """
 
 import ctypes
 
 import pytest
 import torch
+
+from oracle import attention_oracle as AO
 
 pytestmark = pytest.mark.gpu
 
@@ -72,6 +76,12 @@ def test_noalloc_decode_matches_workspace_decode_on_two_calls():
         out = _noalloc(q, kc, vc, idx, cnt, seq, block)
         torch.cuda.synchronize()
         d = (out.float() - ref.float()).abs()
+        assert d.max().item() <= MAX_ABS, d.max().item()
+        assert d.mean().item() <= MEAN_ABS, d.mean().item()
+        # and against the oracle, so a fault shared by both entry points
+        # (they run the same split and merge code) cannot hide
+        want = AO.sparse_decode_fp32(q.cpu(), kc.cpu(), vc.cpu(), idx.cpu(), cnt.cpu(), seq.cpu(), block)
+        d = (out.float().cpu() - want).abs()
         assert d.max().item() <= MAX_ABS, d.max().item()
         assert d.mean().item() <= MEAN_ABS, d.mean().item()
 
