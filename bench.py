@@ -68,6 +68,20 @@ def mask_text(mask, topk) -> str:
             + (f", pooled top-{topk} per layer/head" if topk else ", structure lists only"))
 
 
+def workload_text(name: str) -> str:
+    """The job both arms run, independent of the rank and of the arm."""
+    mask, topk = mask_cfg(name)
+    arch, prompts, scaling = workload(name, 0, 1)
+    if name == "c2":
+        lens = [p[0] for p in prompts]
+        job = f"{len(lens)} prompts of {min(lens)}-{max(lens)} tokens ({'+'.join(map(str, lens))}) split over the GPUs"
+    elif scaling == "tp":
+        job = f"one {prompts[0][0]}-token prompt per job, heads split over the GPUs"
+    else:
+        job = f"one {prompts[0][0]}-token prompt per GPU"
+    return f"{name}: {arch} LLaMA (random init) sparse prefill, {job}, {mask_text(mask, topk)}"
+
+
 def mask_cfg(name: str):
     """(mask builder parameters, pooled top-k) of a workload."""
     return (MASK_C4, 0) if name == "c4" else (MASK, TOPK)
@@ -296,28 +310,62 @@ def cpu_layer_sample(arch: str, L: int, seed: int, repeats: int = 1, mask=None, 
     return dts, a["num_hidden_layers"], threads
 
 
+def cpu_model_ends(arch: str, L: int, seed: int) -> float:
+    """Seconds of the model's parts outside the decoder layers on the host
+    cores: token embedding of the prompt, rotary tables, the final RMSNorm and
+    the LM head on the last position (the prefill keeps only its logits)."""
+    import torch
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaRMSNorm, LlamaRotaryEmbedding
+    a = ARCH[arch]
+    cfg = LlamaConfig(**a, head_dim=128, max_position_embeddings=16384, rope_theta=100000.0,
+                      rope_scaling={"rope_type": "linear", "factor": 4.0}, rms_norm_eps=1e-6)
+    torch.manual_seed(0)
+    emb = torch.nn.Embedding(a["vocab_size"], a["hidden_size"])
+    norm = LlamaRMSNorm(a["hidden_size"], eps=1e-6)
+    head = torch.nn.Linear(a["hidden_size"], a["vocab_size"], bias=False)
+    rot = LlamaRotaryEmbedding(cfg)
+    ids, _ = prompt_inputs(L, seed)
+    ids = torch.from_numpy(ids)
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        h = emb(ids)
+        rot(h, torch.arange(L).unsqueeze(0))
+        head(norm(h)[:, -1:])
+        return time.perf_counter() - t0
+
+
 def run_reference_arm(args, rank, world):
+    """The reference's CPU path on the host cores, on a bounded sample: each
+    timed step is one decoder layer of the workload's first prompt (fp32,
+    projections, RoPE, the reference's dense-masked attention per head, MLP),
+    so `steps` and `ms_per_step` are the layer calls actually timed. The
+    prompt's prefill time is then the mean layer time x the layer count plus
+    the model's ends (embedding, final norm, LM head on the last position,
+    timed once), and `value` = prompt tokens / that time."""
     if rank != 0:
         return
     arch, prompts, scaling = workload(args.workload, 0, 1)
     arch = arch or "1.3b"
     L, seed = prompts[0]
-    # warm-up calls are folded into the same sample run and discarded
     mask, topk = mask_cfg(args.workload)
-    dts, layers, threads = cpu_layer_sample(arch, L, seed, repeats=min(args.warmup, 1) + args.steps, mask=mask,
-                                            topk=topk)
-    times = [d * layers for d in dts[min(args.warmup, 1):]]
-    per_prompt = statistics.mean(times)
+    nwarm = min(args.warmup, 1)
+    dts, layers, threads = cpu_layer_sample(arch, L, seed, repeats=nwarm + args.steps, mask=mask, topk=topk)
+    timed = dts[nwarm:]
+    ends = cpu_model_ends(arch, L, seed)
+    per_layer = statistics.mean(timed)
+    per_prompt = per_layer * layers + ends
     value = L / per_prompt
+    sample = (f"{len(timed)} timed calls of 1 of {layers} decoder layers (fp32, dense-masked SDPA per head) on one "
+              f"{L}-token prompt, {per_layer:.3f} s each, x{layers} + {ends * 1e3:.1f} ms of embedding, final norm "
+              f"and LM head = {per_prompt:.1f} s per prompt")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_prompt * 1e3, "higher_is_better": True,
+        "steps": len(timed), "warmup": nwarm, "ms_per_step": per_layer * 1e3, "higher_is_better": True,
         "scaling": "strong" if scaling == "tp" else scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {arch} LLaMA prefill, {L} tokens, {mask_text(mask, topk)}",
-                   "seq_len": L, "global_batch": 1},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"1 of {layers} decoder layers (fp32, dense-masked SDPA per head) on {L} "
-                                   f"tokens, scaled x{layers}; embeddings/lm_head excluded"},
+        "config": {"workload": workload_text(args.workload), "seq_len": L, "global_batch": 1,
+                   "step": "one decoder layer of one prompt (a bounded sample of the prefill)"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -440,10 +488,11 @@ def run_ours(args, rank, world, dist):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         L0, seed0 = prompts[0]
         dts, layers, threads = cpu_layer_sample(arch, L0, seed0, mask=mask, topk=topk)
-        v = L0 / (dts[0] * layers)
+        ends = cpu_model_ends(arch, L0, seed0)
+        v = L0 / (dts[0] * layers + ends)
         cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
                "sample": f"1 of {layers} decoder layers (fp32, dense-masked SDPA per head) on {L0} tokens, "
-                         f"scaled x{layers}; embeddings/lm_head excluded"}
+                         f"scaled x{layers}, + embedding, final norm and LM head ({ends * 1e3:.1f} ms)"}
 
     weight_gb = sum(p.numel() * p.element_size() for p in model.parameters()) / 1e9
     if rank == 0:
@@ -451,9 +500,8 @@ def run_ours(args, rank, world, dist):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "strong" if scaling == "tp" else scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"{args.workload}: {arch} LLaMA (random-init bf16) sparse prefill, "
-                                   f"{'+'.join(str(p[0]) for p in prepared)} tokens "
-                                   f"{'per job' if tp else 'per GPU'}, {mask_text(mask, topk)}",
+            "config": {"workload": workload_text(args.workload),
+                       "prompts_this_rank": "+".join(str(p[0]) for p in prepared),
                        "seq_len": prepared[0][0], "global_batch": len(prompts) * (world if scaling == "weak" else 1),
                        "parallelism": (f"head-parallel TP x{world} with sequence parallelism: NCCL reduce-scatter "
                                        f"after o_proj and down_proj, all-gather before attention and MLP"

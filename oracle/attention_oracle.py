@@ -25,7 +25,7 @@ Only tests, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
 from __future__ import annotations
 
 import math
-from typing import Optional
+from typing import Optional, Sequence
 
 import numpy as np
 import torch
@@ -43,44 +43,102 @@ def _block_mask_from_lists(idx: torch.Tensor, cnt: torch.Tensor, nb: int) -> tor
 
 
 def sparse_prefill_fp32(q, k, v, block_indices, block_counts, block_size: int,
-                        scale: Optional[float] = None) -> torch.Tensor:
+                        scale: Optional[float] = None, heads: Optional[Sequence[int]] = None,
+                        row_chunk: int = 2048) -> torch.Tensor:
     """Block-sparse causal attention in fp32.
 
     q: ``[B, Hq, L, D]``; k, v: ``[B, Hkv, L, D]``;
     block_indices: ``[B, nb, max]`` (shared by all heads, as in the reference)
     or ``[B, Hq, nb, max]`` (per head); block_counts matching without the last
-    dim. Returns fp32 ``[B, Hq, L, D]``."""
-    q = torch.as_tensor(q).float()
-    k = torch.as_tensor(k).float()
-    v = torch.as_tensor(v).float()
+    dim. Returns fp32 ``[B, Hq, L, D]``, or ``[B, len(heads), L, D]`` for the
+    listed query heads only when ``heads`` is given.
+
+    Rows are processed ``row_chunk`` at a time against the keys up to the
+    chunk's last row (causality), so memory stays bounded at long L; every
+    row's softmax still spans all of its allowed keys at once."""
+    q = torch.as_tensor(q)
+    k = torch.as_tensor(k)
+    v = torch.as_tensor(v)
     Bsz, Hq, L, D = q.shape
     Hkv = k.shape[1]
     g = Hq // Hkv
-    if g > 1:
-        k = k.repeat_interleave(g, dim=1)
-        v = v.repeat_interleave(g, dim=1)
     nb = (L + block_size - 1) // block_size
     bi = torch.as_tensor(block_indices)
     bc = torch.as_tensor(block_counts)
     bm = _block_mask_from_lists(bi, bc, nb)  # [B, nb, nb] or [B, H, nb, nb]
     if bm.dim() == 3:
         bm = bm[:, None]
-    tok = bm.repeat_interleave(block_size, -2).repeat_interleave(block_size, -1)[..., :L, :L]
-    causal = torch.ones(L, L, dtype=torch.bool).tril()
-    allowed = tok & causal
     sc = 1.0 / math.sqrt(D) if scale is None else scale
-    out = torch.empty(Bsz, Hq, L, D, dtype=torch.float32)
+    hs = list(range(Hq)) if heads is None else [int(h) for h in heads]
+    out = torch.empty(Bsz, len(hs), L, D, dtype=torch.float32)
     for b in range(Bsz):
-        for h in range(Hq):
-            a = allowed[b, h if allowed.shape[1] > 1 else 0]
-            s = (q[b, h] @ k[b, h].T) * sc
+        for oi, h in enumerate(hs):
+            hk = h // g
+            bmh = bm[b, h if bm.shape[1] > 1 else 0]
+            kf = k[b, hk].float()
+            vf = v[b, hk].float()
+            for r0 in range(0, L, row_chunk):
+                r1 = min(L, r0 + row_chunk)
+                rows = torch.arange(r0, r1)
+                keys = torch.arange(r1)
+                # token (row, key) allowed: its block pair is listed and key <= row
+                a = bmh[rows // block_size][:, keys // block_size] & (keys[None, :] <= rows[:, None])
+                s = (q[b, h, r0:r1].float() @ kf[:r1].T) * sc
+                s = s.masked_fill(~a, float("-inf"))
+                mx = s.max(-1, keepdim=True).values
+                mx = torch.where(torch.isinf(mx), torch.zeros_like(mx), mx)
+                p = torch.exp(s - mx)
+                l = p.sum(-1, keepdim=True)
+                l = torch.where(l == 0, torch.ones_like(l), l)
+                out[b, oi, r0:r1] = (p @ vf[:r1]) / l
+    return out
+
+
+def sparse_prefill_fp32_gathered(q, k, v, block_indices, block_counts, block_size: int,
+                                 scale: Optional[float] = None) -> torch.Tensor:
+    """The same attention as :func:`sparse_prefill_fp32` for lists shared by
+    all heads (``[B, nb, max]``, the reference's layout), computed only over
+    the listed key blocks: for each query block the keys of its listed
+    blocks ``<=`` the query block are gathered (in ascending block order) and
+    every head's rows take a masked softmax over them (key ``<=`` row), in
+    fp32, all heads at once. Fully masked rows give zeros. This is the
+    kernel's own loop structure (``sabrecoder_attention_triton.py:70-112``:
+    one query block against its listed key blocks), used where the dense
+    form would be too slow on the host (whole-model runs at 12K+ tokens)."""
+    q = torch.as_tensor(q)
+    k = torch.as_tensor(k)
+    v = torch.as_tensor(v)
+    Bsz, Hq, L, D = q.shape
+    Hkv = k.shape[1]
+    g = Hq // Hkv
+    nb = (L + block_size - 1) // block_size
+    bi = torch.as_tensor(block_indices)
+    bc = torch.as_tensor(block_counts)
+    if bi.dim() != 3:
+        raise ValueError("sparse_prefill_fp32_gathered: lists must be shared by all heads, [B, nb, max]")
+    bm = _block_mask_from_lists(bi, bc, nb)  # [B, nb, nb]
+    sc = 1.0 / math.sqrt(D) if scale is None else scale
+    out = torch.zeros(Bsz, Hq, L, D, dtype=torch.float32)
+    for b in range(Bsz):
+        kf = k[b].float().repeat_interleave(g, dim=0) if g > 1 else k[b].float()
+        vf = v[b].float().repeat_interleave(g, dim=0) if g > 1 else v[b].float()
+        for qb in range(nb):
+            r0, r1 = qb * block_size, min(L, (qb + 1) * block_size)
+            kbs = torch.nonzero(bm[b, qb, :qb + 1]).flatten()
+            if kbs.numel() == 0:
+                continue
+            keys = (kbs[:, None] * block_size + torch.arange(block_size)[None, :]).flatten()
+            keys = keys[keys < L]
+            rows = torch.arange(r0, r1)
+            a = keys[None, :] <= rows[:, None]
+            s = (q[b, :, r0:r1].float() @ kf[:, keys].transpose(-1, -2)) * sc  # [H, rows, keys]
             s = s.masked_fill(~a, float("-inf"))
             mx = s.max(-1, keepdim=True).values
             mx = torch.where(torch.isinf(mx), torch.zeros_like(mx), mx)
             p = torch.exp(s - mx)
             l = p.sum(-1, keepdim=True)
             l = torch.where(l == 0, torch.ones_like(l), l)
-            out[b, h] = (p @ v[b, h]) / l
+            out[b, :, r0:r1] = (p @ vf[:, keys]) / l
     return out
 
 

@@ -6,7 +6,9 @@ Restates ``StructureAwareAttentionWrapperTriton.forward``
 "hybrid" mode: q/k/v projections, HF rotary embedding (:292-293), cache
 update (:295-299), GQA ``repeat_interleave`` (:301-303), dense SDPA for
 one-token decode (:305-308, :254-268) and the block-sparse prefill
-(:309-313) computed by :func:`oracle.attention_oracle.sparse_prefill_fp32`.
+(:309-313) computed by :func:`oracle.attention_oracle.sparse_prefill_fp32`
+(or its gathered form, :func:`oracle.attention_oracle.sparse_prefill_fp32_gathered`,
+when the lists are shared by all heads as in the reference).
 """
 
 from __future__ import annotations
@@ -14,7 +16,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from .attention_oracle import sparse_prefill_fp32
+from .attention_oracle import sparse_prefill_fp32, sparse_prefill_fp32_gathered
 
 
 class OracleAttention(nn.Module):
@@ -46,7 +48,9 @@ class OracleAttention(nn.Module):
         if L == 1:
             o = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=False)
         else:
-            o = sparse_prefill_fp32(q, k, v, self.bi, self.bc, self.block).to(q.dtype)
+            shared = torch.as_tensor(self.bi).dim() == 3
+            fn = sparse_prefill_fp32_gathered if shared else sparse_prefill_fp32
+            o = fn(q, k, v, self.bi, self.bc, self.block).to(q.dtype)
         o = o.transpose(1, 2).reshape(B, L, -1)
         return self.o_proj(o), None
 

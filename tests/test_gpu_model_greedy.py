@@ -1,0 +1,98 @@
+"""Greedy tokens of the patched 1.3B model against the oracle model.
+
+The deepseek-coder-1.3B architecture (24 layers, hidden 2048, 16 heads x 128,
+MLP 5504, vocab 32256, RoPE theta 1e5 linear x4), random-init bf16 weights, a
+12288-token prompt with the benchmark's structure spans and mask parameters,
+block-sparse prefill with the structure lists (the reference's configuration:
+no top-k extension) and dense decode, as the reference's evaluator runs it
+(methods/sabrecoder/run_eval.py:340-348; wrapper
+sabrecoder_llama_triton.py:270-319, dense decode :305-308).
+
+The patched model generates 32 greedy tokens free-running on the GPU (its own
+token is fed back every step, through the preallocated cache). The oracle
+model -- the same bf16 weights on the host, the oracle's attention in fp32 --
+is then run over that sequence and must pick the same token at every step:
+if it does, its own free-running greedy sequence is the same 32 tokens. Both
+LM heads compute in fp32 so rounding logits to bf16 cannot create exact ties.
+The first step where they differ (if any), the oracle's top-1/top-2 margin
+there and the smallest margin seen are reported.
+"""
+
+import copy
+
+import pytest
+import torch
+
+import bench
+
+pytestmark = pytest.mark.gpu
+
+STEPS = 32
+PROMPT = 12288
+
+
+def _fp32_head(model):
+    model.lm_head.float()
+    model.lm_head.register_forward_pre_hook(lambda mod, args: (args[0].float(),))
+
+
+@pytest.mark.timeout(1800)
+def test_greedy_tokens_match_oracle_on_1p3b_at_12k():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from oracle.llama_oracle import patch_oracle
+    from sabrecoder_b200 import sabrecoder_llama as SL
+    from sabrecoder_b200.kv_cache import SabreKVCache
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+    from transformers import DynamicCache
+
+    dev = torch.device("cuda")
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    model, cfg = bench.build_model("1.3b", dev)
+    ref = copy.deepcopy(model).to("cpu")
+    _fp32_head(model)
+    _fp32_head(ref)
+    mask = bench.MASK
+    SL.patch_model_with_sabrecoder_attention(model, None, topk_blocks=0, verbose=False, **mask)
+    ids, spans = bench.prompt_inputs(PROMPT, 1000, cfg.vocab_size)
+    mb = StructureAwareMaskBuilder(None, **mask)
+    bi, bc, bm = mb.build_block_indices_from_spans(spans, dev)
+    patch_oracle(ref, bi.cpu(), bc.cpu(), mask["block_size"])
+    ids_t = torch.from_numpy(ids)
+
+    SL.set_current_code("<synthetic prompt>")
+    SL.set_precomputed_blocks(bi, bc)
+    ours = []
+    try:
+        with torch.no_grad():
+            cache = SabreKVCache(cfg, batch_size=1, max_cache_len=PROMPT + STEPS + 64, device=dev)
+            logits = model(input_ids=ids_t.to(dev), past_key_values=cache, use_cache=True,
+                           logits_to_keep=1).logits
+            for _ in range(STEPS):
+                tok = int(logits[0, -1].float().argmax())
+                ours.append(tok)
+                logits = model(input_ids=torch.tensor([[tok]], device=dev), past_key_values=cache,
+                               use_cache=True).logits
+    finally:
+        SL.clear_current_code()
+        SL.clear_precomputed_blocks()
+    del model
+    torch.cuda.empty_cache()
+
+    rows = []  # (step, ours, oracle argmax, oracle top1-top2 margin, oracle top1 - logit[ours])
+    with torch.no_grad():
+        cc = DynamicCache()
+        lb = ref(input_ids=ids_t, past_key_values=cc, use_cache=True, logits_to_keep=1).logits
+        for step, tok in enumerate(ours):
+            b = lb[0, -1].float()
+            top2 = b.topk(2)
+            rows.append((step, tok, int(top2.indices[0]), (top2.values[0] - top2.values[1]).item(),
+                         (top2.values[0] - b[tok]).item()))
+            lb = ref(input_ids=torch.tensor([[tok]]), past_key_values=cc, use_cache=True).logits
+    first = next((r for r in rows if r[1] != r[2]), None)
+    report = (f"tokens {ours}; first divergence: "
+              f"{'none' if first is None else f'step {first[0]} (ours {first[1]}, oracle {first[2]}, oracle margin {first[3]:.4f}, gap {first[4]:.4f})'}; "
+              f"smallest oracle top-1 margin {min(r[3] for r in rows):.4f} at step "
+              f"{min(rows, key=lambda r: r[3])[0]}")
+    print(report)
+    assert first is None, report

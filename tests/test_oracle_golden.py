@@ -84,6 +84,16 @@ def test_prefill_oracle_matches_reference_kernel(case):
                                  torch.from_numpy(g["block_counts"]), int(g["block_size"]))
     ref = torch.from_numpy(g["out"])
     assert (out - ref).abs().max().item() < 2e-5
+    # the gathered form (listed blocks only, used for whole-model runs)
+    out_g = AO.sparse_prefill_fp32_gathered(q, k, v, torch.from_numpy(g["block_indices"]),
+                                            torch.from_numpy(g["block_counts"]), int(g["block_size"]))
+    assert (out_g - ref).abs().max().item() < 2e-5
+    # and a head subset of the row-chunked form
+    H = q.shape[1]
+    sub = AO.sparse_prefill_fp32(q, k, v, torch.from_numpy(g["block_indices"]),
+                                 torch.from_numpy(g["block_counts"]), int(g["block_size"]), heads=[H - 1],
+                                 row_chunk=100)
+    assert (sub[:, 0] - ref[:, H - 1]).abs().max().item() < 2e-5
 
 
 def test_sparsity_utils_values(golden_dir):
