@@ -47,6 +47,17 @@ const char* sabre_last_error(void);
  * Synchronises `stream`. */
 int sabre_device_status(unsigned int* flags_out, int clear, void* stream);
 
+/* Limit, in nanoseconds, of every bounded wait in the kernels' main loops on
+ * the current device (default 2 s; ns = 0 restores it; otherwise 1 us <= ns
+ * <= 60 s). Applies to kernels launched after the call (synchronous). A wait
+ * that runs out records SABRE_DEV_TIMEOUT, the CTA drains the copies and
+ * MMAs it issued (those drains always allow 2 s), frees its tensor memory and
+ * exits without writing its output tile. A limit shorter than a kernel's
+ * normal waits makes correct calls fail this way: it is meant for tests of
+ * the timeout path and for callers that want a tighter watchdog. No
+ * counterpart in the reference (its Triton kernels have no bounded waits). */
+int sabre_set_wait_limit_ns(unsigned long long ns);
+
 /* ------------------------------------------------------------------------
  * (1) Block-sparse prefill attention.
  *

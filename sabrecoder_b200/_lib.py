@@ -24,6 +24,7 @@ SIGNATURES = {
     "sabre_status_string": (ctypes.c_char_p, [c_int]),
     "sabre_last_error": (ctypes.c_char_p, []),
     "sabre_device_status": (c_int, [ctypes.POINTER(c_uint), c_int, P]),
+    "sabre_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong]),
     "sabre_prefill_bsa": (c_int, [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                   I64P, I64P, I64P, I64P, I64P, I64P, c_float, c_int, P]),
     "sabre_decode_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),

@@ -43,6 +43,12 @@ __device__ unsigned int g_device_status;
 
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 
+// Limit of the bounded waits in the kernels' main loops (one per loaded
+// library and device), kWaitNs unless sabre_set_wait_limit_ns changed it.
+// The drain waits after an abort (mbar_wait_drain) always allow kWaitNs, so a
+// short limit can never let a CTA exit before its own copies and MMAs land.
+__device__ unsigned long long g_wait_limit_ns = kWaitNs;
+
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -105,10 +111,17 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
   if (mbar_test_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
+  const unsigned long long lim = *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+  // At the default limit a poll may suspend the thread (try_wait) and the
+  // clock is read every 64 polls. Under a shorter limit the polls never
+  // suspend (test_wait) and the clock is read after each, so the limit holds
+  // to within a poll.
+  const bool short_limit = lim < kWaitNs;
+  const uint32_t every = short_limit ? 0u : 63u;
   for (uint32_t i = 0;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (short_limit ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if ((i & 63u) == 63u && globaltimer_ns() - t0 > kWaitNs) {
+    if ((i & every) == every && globaltimer_ns() - t0 > lim) {
       record_status(SABRE_DEV_TIMEOUT);
       *abort = 1;
       return false;

@@ -132,6 +132,14 @@ int sabre_device_status(unsigned int* flags_out, int clear, void* stream) {
   return SABRE_OK;
 }
 
+int sabre_set_wait_limit_ns(unsigned long long ns) {
+  if (ns != 0 && (ns < 1000ull || ns > 60000000000ull))
+    return fail(SABRE_ERR_INVALID_ARG, "sabre_set_wait_limit_ns: %llu ns outside [1 us, 60 s] (0 = default)", ns);
+  const unsigned long long v = ns == 0 ? kWaitNs : ns;
+  SABRE_CUDA_TRY(cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v)));
+  return SABRE_OK;
+}
+
 }  // extern "C"
 
 namespace sabre {

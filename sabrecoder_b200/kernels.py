@@ -142,8 +142,8 @@ def rope_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tenso
     if tuple(k_out.shape[:2]) != (B, Hkv) or k_out.shape[3] != D:
         raise SabreError(f"rope_qkv: k_out/v_out {tuple(k_out.shape)} do not match [B={B}, Hkv={Hkv}, T, D={D}]")
     if cos.dim() not in (2, 3) or sin.shape != cos.shape or cos.shape[-1] != D or cos.shape[-2] < L or (
-            cos.dim() == 3 and cos.shape[0] != B):
-        raise SabreError(f"rope_qkv: cos/sin {tuple(cos.shape)} must be [B, >= L, D] or [>= L, D] "
+            cos.dim() == 3 and cos.shape[0] not in (1, B)):
+        raise SabreError(f"rope_qkv: cos/sin {tuple(cos.shape)} must be [B or 1, >= L, D] or [>= L, D] "
                          f"(B={B}, L={L}, D={D})")
     _need_cuda(q=q, k=k, v=v, cos=cos, sin=sin, k_out=k_out, v_out=v_out)
     if q.dtype not in DTYPE_CODE or any(t.dtype != q.dtype for t in (k, v, cos, sin, k_out, v_out)):
@@ -151,10 +151,13 @@ def rope_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tenso
     if q_out is None:
         q_out = q
     if cos.dim() == 2:
-        cos = cos.unsqueeze(0).expand(B, -1, -1)
-        sin = sin.unsqueeze(0).expand(B, -1, -1)
+        cos, sin = cos.unsqueeze(0), sin.unsqueeze(0)
     if cos.stride(-1) != 1 or sin.stride() != cos.stride():
         cos, sin = cos.contiguous(), sin.contiguous()
+    # One table for every sequence (transformers builds [1, L, D] from shared
+    # position ids): batch stride 0, so the kernel never reads past it.
+    if cos.shape[0] != B:
+        cos, sin = cos.expand(B, -1, -1), sin.expand(B, -1, -1)
     qp = kp = None
     if pool_block > 0:
         nb = (L + pool_block - 1) // pool_block
@@ -378,6 +381,14 @@ def device_status(clear: bool = True, stream: Optional[int] = None) -> int:
                                            else None)
     check(lib().sabre_device_status(ctypes.byref(v), 1 if clear else 0, s), "sabre_device_status")
     return int(v.value)
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Limit of the kernels' bounded waits on the current device, in ns
+    (0 restores the default of 2 s). A wait that runs out records
+    SABRE_DEV_TIMEOUT (read with device_status); the kernel drains what it
+    issued and exits without writing its output tile."""
+    check(lib().sabre_set_wait_limit_ns(int(ns)), "sabre_set_wait_limit_ns")
 
 
 # ---------------------------------------------------------------------------

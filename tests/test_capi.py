@@ -118,7 +118,7 @@ def test_rope_qkv_rejects_mismatched_shapes(what):
     if what == "cos_rows":
         cs = torch.zeros(B, L - 1, D, dtype=torch.bfloat16)
     elif what == "cos_batch":
-        cs = torch.zeros(B + 1, L, D, dtype=torch.bfloat16)
+        cs = torch.zeros(B + 1, L, D, dtype=torch.bfloat16)  # neither B nor 1
     elif what == "kout_batch":
         kv = torch.zeros(B - 1, Hkv, T, D, dtype=torch.bfloat16)
     elif what == "kout_heads":

