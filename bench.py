@@ -96,6 +96,7 @@ def parse_args():
     ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c0"], default="c1")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-op16k", action="store_true", help="skip the 16K attention-op roofline record")
     ap.add_argument("--attn-only", action="store_true",
                     help="time the prefill attention kernel alone on one layer of the workload")
     ap.add_argument("--aux-op", choices=["mask", "token", "similarity"], default=None,
@@ -494,6 +495,21 @@ def run_ours(args, rank, world, dist):
                "sample": f"1 of {layers} decoder layers (fp32, dense-masked SDPA per head) on {L0} tokens, "
                          f"scaled x{layers}, + embedding, final norm and LM head ({ends * 1e3:.1f} ms)"}
 
+    # The 16K-token attention op the prefill target is stated for (the c3
+    # layer shape: 32 heads, structure + top-8 lists), timed alone with L2
+    # flushed, so every bench line carries a 16K roofline.
+    roof16 = None
+    if not args.no_op16k:
+        ms16, flop16, dens16, H16, L16 = op_measure("c3", rank, max(3, min(args.steps, 10)), 3)
+        ach16 = flop16 / ms16 / 1e9
+        roof16 = {"kernel": "sabre prefill_bsa_kernel", "bound": "tensor",
+                  "workload": f"attention op B=1 H={H16} L={L16} D=128 block 64, structure + top-{TOPK}, "
+                              f"density {dens16:.4f}, {L2Flush.NOTE}",
+                  "achieved": ach16, "peak": burst, "unit": "TFLOP/s", "frac": ach16 / burst,
+                  "peak_kind": f"{which} bf16 dense, burst (kernel timed alone)",
+                  "frac_of_sustained": ach16 / sustained, "flop_per_launch": flop16, "ms_per_launch": ms16,
+                  "traffic": profile_traffic("prefill_bsa_c3_op")}
+
     weight_gb = sum(p.numel() * p.element_size() for p in model.parameters()) / 1e9
     if rank == 0:
         line = {
@@ -516,6 +532,7 @@ def run_ours(args, rank, world, dist):
                          "peak_kind": f"{which} bf16 dense, sustained (kernel timed inside a long step)",
                          "flop_per_launch": per_launch_flop, "ms_per_launch": per_launch_ms,
                          "traffic": traffic},
+            "roofline_16k": roof16,
             "gpu_launches": launches,
             "clocks": ck,
             "e2e": e2e,
@@ -610,16 +627,18 @@ OP_SHAPES = {"c0": (16, 4096, "spans"), "c1": (16, 12288, "bench"), "c2": (16, 1
              "c3": (32, 16384, "bench")}
 
 
-def run_op_bench(args, rank, world, dist):
-    """The prefill attention op alone on one layer's shape of the workload
+def op_measure(name: str, rank: int, steps: int, warmup: int):
+    """The prefill attention op alone on one layer's shape of a workload
     (c0: B=1, H=16, L=4096; c1: H=16, L=12288; c3: H=32, L=16384), block 64,
-    structure + pooled top-8 lists, L2 flushed between timed launches."""
+    structure + pooled top-8 lists, L2 flushed between timed launches (the
+    flush is outside the timed window). Returns (ms per launch, algorithmic
+    FLOP per launch, density, H, L)."""
     import torch
     from sabrecoder_b200 import kernels as K
     from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
     from sabrecoder_b200.spans import BENCH_SPAN_MIX, make_spans
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
-    H, L, mix = OP_SHAPES[args.workload]
+    H, L, mix = OP_SHAPES[name]
     blk = 64
     g = torch.Generator(device=dev).manual_seed(rank)
     q, k, v = (torch.randn(1, L, H, 128, device=dev, generator=g, dtype=torch.bfloat16).transpose(1, 2)
@@ -633,11 +652,11 @@ def run_op_bench(args, rank, world, dist):
     idx = idx[..., :ma].contiguous()
     out = torch.empty_like(q)
     flush = L2Flush(dev)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         K.prefill_bsa(q, k, v, idx, cnt, blk, out=out)
     torch.cuda.synchronize()
     tot = 0.0
-    for _ in range(args.steps):
+    for _ in range(steps):
         flush()
         s, e = torch.cuda.Event(True), torch.cuda.Event(True)
         s.record()
@@ -645,10 +664,16 @@ def run_op_bench(args, rank, world, dist):
         e.record()
         torch.cuda.synchronize()
         tot += s.elapsed_time(e)
-    ms = tot / args.steps
+    ms = tot / steps
     flop = float(cnt.sum().item()) * 4 * blk * blk * 128
     nb = bm.shape[0]
     dens = float(cnt.sum().item()) / (H * nb * (nb + 1) / 2)
+    return ms, flop, dens, H, L
+
+
+def run_op_bench(args, rank, world, dist):
+    """The prefill attention op alone on one layer's shape of the workload."""
+    ms, flop, dens, H, L = op_measure(args.workload, rank, args.steps, args.warmup)
     burst, sustained, hbm, which = measured_peaks()
     traffic = profile_traffic(f"prefill_bsa_{args.workload}_op")
     if rank == 0:
