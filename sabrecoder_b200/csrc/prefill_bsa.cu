@@ -114,6 +114,45 @@ struct UnionIter {
   }
 };
 
+// Maximum of 64 scores: a tree of three-input maxima (32 instructions, depth 4).
+__device__ __forceinline__ float row_max64(const float (&x)[64]) {
+  float a[22];
+#pragma unroll
+  for (int i = 0; i < 21; ++i) a[i] = fmax3(x[3 * i], x[3 * i + 1], x[3 * i + 2]);
+  a[21] = x[63];
+  float b[8];
+#pragma unroll
+  for (int i = 0; i < 7; ++i) b[i] = fmax3(a[3 * i], a[3 * i + 1], a[3 * i + 2]);
+  b[7] = a[21];
+  return fmax3(fmax3(b[0], b[1], b[2]), fmax3(b[3], b[4], b[5]), fmaxf(b[6], b[7]));
+}
+
+// P = 2^(x * sl2 - moff) for one row of 64 scores (-inf gives 0), packed
+// two per word in the storage type, and the row sum of the fp32 values (four
+// packed partial sums, added in a fixed order). The scale/offset and the sums
+// use the packed f32x2 forms: half the FMA-pipe instructions of scalar code.
+template <typename T>
+__device__ __forceinline__ float exp_tile(const float (&x)[64], float sl2, float moff, uint32_t (&pk)[32]) {
+  const uint64_t sc = f2_pack(sl2, sl2);
+  const uint64_t off = f2_pack(-moff, -moff);
+  uint64_t acc[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i] = f2_pack(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float y0, y1;
+    f2_unpack(f2_fma(f2_pack(x[2 * i], x[2 * i + 1]), sc, off), y0, y1);
+    const float p0 = ex2(y0);
+    const float p1 = ex2(y1);
+    acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
+    pk[i] = DT<T>::pack(p0, p1);
+  }
+  float s[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f2_unpack(acc[i], s[2 * i], s[2 * i + 1]);
+  return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
+}
+
 // kTok: also apply the token-level masks of the listed blocks (Params::tmask).
 template <typename T, bool kTok>
 __global__ void __launch_bounds__(kThreads, 2)
@@ -330,29 +369,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < 64; ++c)
           if (c >= nvalid || !((tw >> c) & 1ull)) x[c] = -INFINITY;
       }
-      // Row max as 8 independent chains, then a tree (short dependency chain).
-      float m8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = x[i];
-#pragma unroll
-      for (int c = 8; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], x[c]);
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      const float mx = row_max64(x);
       const float m_tile = mx * sl2;
       const bool rescale = m_tile > m_run + 8.0f;
       const float m_use = rescale ? m_tile : m_run;
       const float alpha = rescale ? ex2(m_run - m_use) : 1.0f;
       const float moff = (m_use == -INFINITY) ? 0.0f : m_use;
-      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t pk[32];
-#pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        const float p0 = ex2(fmaf(x[c], sl2, -moff));
-        const float p1 = ex2(fmaf(x[c + 1], sl2, -moff));
-        s8[(c >> 1) & 7] += p0 + p1;
-        pk[c >> 1] = DT<T>::pack(p0, p1);
-      }
-      const float rs = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+      const float rs = exp_tile<T>(x, sl2, moff, pk);
       l_run = l_run * alpha + rs;
       m_run = m_use;
 

@@ -10,24 +10,30 @@ sabrecoder_llama_triton.py:270-319, dense decode :305-308).
 
 The patched model generates 32 greedy tokens free-running on the GPU (its own
 token is fed back every step, through the preallocated cache). The oracle
-model -- the same bf16 weights on the host, the oracle's attention in fp32 --
-is then run over that sequence (prompt plus our tokens), so at every step both
-models see the same prefix. At each step:
+model is then run over that sequence (prompt plus our tokens), so at every
+step it sees the same prefix, twice on the host with the same weights:
 
-* the logits agree within 3 % of the largest oracle logit magnitude (the two
-  models differ by bf16 GEMM accumulation order and by P rounding in the
-  attention kernel), and
-* our token is the oracle's greedy choice, or the oracle scores it within
-  that same bound of its own top-1 (a numerical tie: random-init weights give
-  top-1/top-2 margins down to ~1e-3 of a logit scale of ~5, below the bf16
-  noise of any two implementations, so the greedy choice there is decided by
-  rounding).
+* in fp32 (weights widened exactly, the oracle's attention in fp32): the
+  exact reference, against which both bf16 computations are measured;
+* in bf16, the way the reference itself runs the model: its distance from
+  the fp32 run is the reference's own bf16 rounding noise on this model.
 
-Where every step is the oracle's own choice, the oracle's free-running greedy
-sequence equals ours. The test prints the first step where the choices
-differ (if any), the oracle's margin there, the smallest margin seen and the
-largest logit error. Both LM heads compute in fp32, so rounding logits to
-bf16 cannot create exact ties.
+Random-init weights give top-1/top-2 logit margins down to ~1e-3 (logit scale
+~3), below the bf16 noise of any implementation, so an exact greedy choice
+can only be asked for where the margin exceeds that noise. At every step:
+
+* our logits are within NOISE_FACTOR x the reference's own bf16 noise of
+  the exact logits (largest absolute difference over the vocabulary, the
+  noise taken as its largest value over the 32 steps), and
+* our token is the exact greedy choice, or the exact logits score it within
+  that bound of their top-1 (a tie at bf16 precision).
+
+Where every step is the exact greedy choice, the exact model's free-running
+greedy sequence equals ours. The test prints the first step where the
+choices differ (if any), the exact margin there, the smallest and median
+margins, the logit errors, and how often the reference's own bf16 run
+departs from the exact greedy choice on the same prefixes. Both LM heads
+compute in fp32, so rounding logits to bf16 cannot create exact ties.
 """
 
 import copy
@@ -41,7 +47,7 @@ pytestmark = pytest.mark.gpu
 
 STEPS = 32
 PROMPT = 12288
-REL = 0.03
+NOISE_FACTOR = 2.0
 
 
 def _fp32_head(model):
@@ -94,26 +100,39 @@ def test_greedy_tokens_match_oracle_on_1p3b_at_12k():
     del model
     torch.cuda.empty_cache()
 
-    # (step, ours, oracle argmax, oracle top1-top2 margin, oracle top1 - oracle[ours], logit error, bound)
-    rows = []
-    with torch.no_grad():
-        cc = DynamicCache()
-        lb = ref(input_ids=ids_t, past_key_values=cc, use_cache=True, logits_to_keep=1).logits
-        for step, tok in enumerate(ours):
-            b = lb[0, -1].float()
-            top2 = b.topk(2)
-            bound = REL * b.abs().max().item()
-            rows.append((step, tok, int(top2.indices[0]), (top2.values[0] - top2.values[1]).item(),
-                         (top2.values[0] - b[tok]).item(), (ours_logits[step] - b).abs().max().item(), bound))
-            lb = ref(input_ids=torch.tensor([[tok]]), past_key_values=cc, use_cache=True).logits
-    differ = [r for r in rows if r[1] != r[2]]
+    def teacher_forced(m):
+        """Logits (fp32, [steps, vocab]) of model m over the prompt and our tokens."""
+        out = []
+        with torch.no_grad():
+            cc = DynamicCache()
+            lb = m(input_ids=ids_t, past_key_values=cc, use_cache=True, logits_to_keep=1).logits
+            for tok in ours:
+                out.append(lb[0, -1].float())
+                lb = m(input_ids=torch.tensor([[tok]]), past_key_values=cc, use_cache=True).logits
+        return torch.stack(out)
+
+    ref16 = teacher_forced(ref)
+    ref.float()
+    ref32 = teacher_forced(ref)
+    a = torch.stack(ours_logits)
+    err_ours = (a - ref32).abs().amax(-1)
+    err_ref = (ref16 - ref32).abs().amax(-1)
+    bound = NOISE_FACTOR * err_ref.max().item()
+    top2 = ref32.topk(2, dim=-1)
+    margin = (top2.values[:, 0] - top2.values[:, 1])
+    exact = top2.indices[:, 0]
+    toks = torch.tensor(ours)
+    gap = top2.values[:, 0] - ref32.gather(1, toks[:, None])[:, 0]
+    differ = [i for i in range(STEPS) if int(toks[i]) != int(exact[i])]
+    ref_differ = [i for i in range(STEPS) if int(ref16[i].argmax()) != int(exact[i])]
     first = differ[0] if differ else None
-    report = (f"tokens {ours}; steps where the oracle's greedy choice differs: {len(differ)} "
-              f"(first: {'none' if first is None else f'step {first[0]}, ours {first[1]}, oracle {first[2]}, oracle top-2 margin {first[3]:.4f}, oracle gap to ours {first[4]:.4f}, bound {first[6]:.4f}'}); "
-              f"oracle top-2 margins min {min(r[3] for r in rows):.4f} / median "
-              f"{sorted(r[3] for r in rows)[len(rows) // 2]:.4f}; largest logit error "
-              f"{max(r[5] for r in rows):.4f} against bounds >= {min(r[6] for r in rows):.4f}")
+    report = (f"tokens {ours}; steps where ours differs from the exact greedy choice: {differ} "
+              f"(first: {'none' if first is None else f'step {first}, ours {ours[first]}, exact {int(exact[first])}, exact top-2 margin {margin[first]:.4f}, exact gap to ours {gap[first]:.4f}'}); "
+              f"the reference's own bf16 run differs at {ref_differ}; exact top-2 margins min {margin.min():.4f} / "
+              f"median {margin.median():.4f}; logit error ours max {err_ours.max():.4f} / median "
+              f"{err_ours.median():.4f}, reference bf16 max {err_ref.max():.4f} / median {err_ref.median():.4f}; "
+              f"bound {bound:.4f}")
     print(report)
-    assert all(r[5] < r[6] for r in rows), report
-    assert all(r[4] < r[6] for r in differ), report
+    assert (err_ours <= bound).all(), report
+    assert all(gap[i].item() <= bound for i in differ), report
     assert len(differ) <= STEPS // 4, report
