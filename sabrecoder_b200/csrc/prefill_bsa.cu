@@ -91,6 +91,7 @@ struct Params {
   long long idx_sb, idx_sh, idx_sm, idx_sk;
   long long cnt_sb, cnt_sh, cnt_sm;
   int B, Hq, Hkv, L, block, max_active, ntiles, nkt;
+  int head_major;  // grid (tiles, B*Hq) instead of (B*Hq, tiles)
   float scale_log2;
 };
 
@@ -168,12 +169,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kMiscOff + 4);
   auto bar = [&](int i) -> uint32_t { return sbase + kBarOff + 8u * i; };
 
-  const int bh = blockIdx.x;
+  // Heaviest (last) query tiles first: later rows list more key blocks.
+  // Row-major (grid x = head): the heaviest tiles of all heads run first,
+  // the best tail. Head-major (grid x = tile, for K/V larger than L2): the
+  // tiles of one head run together, so the K/V rows of the few heads in
+  // flight stay in L2 instead of being re-read from HBM.
+  const int bh = p.head_major ? static_cast<int>(blockIdx.y) : static_cast<int>(blockIdx.x);
   const int b = bh / p.Hq;
   const int h = bh - b * p.Hq;
   const int hk = h / (p.Hq / p.Hkv);
-  // Heaviest (last) query tiles first: later rows list more key blocks.
-  const int tile = p.ntiles - 1 - static_cast<int>(blockIdx.y);
+  const int tile = p.ntiles - 1 - static_cast<int>(p.head_major ? blockIdx.x : blockIdx.y);
   const int r0 = tile * kTileM;
 
   if (tid == 0) {

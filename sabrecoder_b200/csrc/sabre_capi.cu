@@ -213,9 +213,15 @@ static int prefill_launch(const void* q, const void* k, const void* v, void* o, 
   const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(head_dim));
   p.scale_log2 = scale * 1.4426950408889634f;
 
-  if ((long long)batch * heads_q > 2147483647ll || p.ntiles > 65535)
+  // K/V of every head larger than this -> head-major CTA order (measured on
+  // B200, 126 MB L2: c1's 101 MB runs 3.6 % faster row-major, c3's 268 MB
+  // 1.7 % faster head-major, with DRAM reads 3.6x -> 1.0x the algorithmic).
+  const long long kv_bytes = 2ll * batch * heads_kv * seq_len * head_dim * 2;
+  p.head_major = kv_bytes > (112ll << 20) ? 1 : 0;
+  if ((long long)batch * heads_q > 2147483647ll || (p.head_major && (long long)batch * heads_q > 65535ll) ||
+      p.ntiles > 65535)
     return fail(SABRE_ERR_UNSUPPORTED, "sabre_prefill_bsa: grid too large");
-  dim3 grid(batch * heads_q, p.ntiles);
+  dim3 grid = p.head_major ? dim3(p.ntiles, batch * heads_q) : dim3(batch * heads_q, p.ntiles);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tok = (tmask != nullptr);
   if (dtype == SABRE_BF16 && !tok) {
