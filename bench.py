@@ -101,6 +101,9 @@ def parse_args():
                     help="time the prefill attention kernel alone on one layer of the workload")
     ap.add_argument("--aux-op", choices=["mask", "token", "similarity"], default=None,
                     help="time one of the structure-side GPU paths on the workload's prompt (c1 shape)")
+    ap.add_argument("--prefill-op", choices=["qkv"], default=None,
+                    help="time the fused prefill q/k/v projection + RoPE + KV store + pooling against the "
+                         "unfused sequence (three cuBLAS projections, then the RoPE/KV kernel) on one layer")
     ap.add_argument("--decode-op", choices=["dense", "sparse", "qkv"], default=None,
                     help="time the decode attention kernel alone on one layer of the workload: over every cached "
                          "block (dense) or over the last prompt row's list plus the generated blocks (sparse)")
@@ -386,6 +389,8 @@ def run_ours(args, rank, world, dist):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     arch, prompts, scaling = workload(args.workload, rank, world)
+    if args.prefill_op == "qkv":
+        return run_qkv_prefill_op(args, rank, world, dist)
     if args.decode_op == "qkv":
         return run_qkv_op(args, rank, world, dist)
     if args.decode_op:
@@ -927,6 +932,80 @@ def run_qkv_op(args, rank, world, dist):
                                        "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                                        "peak_kind": f"{which} HBM copy bandwidth", "bytes_per_launch": nbytes,
                                        "ms_per_launch": times["fused"], "traffic": None}}))
+
+
+# (hidden, query heads, KV heads, prompt tokens) of one prefill layer on one GPU.
+PREFILL_QKV_SHAPES = {"c1": (2048, 16, 16, 12288), "c3": (4096, 32, 32, 16384), "c4": (7168, 56, 8, 16384)}
+
+
+def run_qkv_prefill_op(args, rank, world, dist):
+    """One prompt's q/k/v projection + RoPE + KV store (+ pooling by 64 when the
+    workload uses the pooled top-k) on one layer's shape: the fused kernel
+    (sabre_qkv_proj_rope) against the unfused sequence (three cuBLAS
+    projections, then sabre_rope_qkv), L2 flushed between launches. FLOPs
+    counted: the projection, 2 x L x N x hidden."""
+    import torch
+    from sabrecoder_b200 import kernels as K
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    hidden, Hq, Hkv, L = PREFILL_QKV_SHAPES.get(args.workload, PREFILL_QKV_SHAPES["c1"])
+    _, topk = mask_cfg(args.workload)
+    pool = 64 if topk else 0
+    D = 128
+    N = (Hq + 2 * Hkv) * D
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = (torch.randn(1, L, hidden, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, hidden, device=dev, generator=g) / hidden ** 0.5).to(torch.bfloat16)
+    wq, wk, wv = w[:Hq * D], w[Hq * D:(Hq + Hkv) * D], w[(Hq + Hkv) * D:]
+    ang = torch.rand(1, L, D // 2, device=dev, generator=g) * 50
+    emb = torch.cat([ang, ang], -1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    kc = torch.zeros(1, Hkv, L + 64, D, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    q_out = torch.empty(1, L, Hq, D, dtype=torch.bfloat16, device=dev)
+
+    def fused():
+        K.qkv_proj_rope(x, w, cos, sin, q_out, kc, vc, pool_block=pool)
+
+    def unfused():
+        q = torch.nn.functional.linear(x, wq).view(1, L, Hq, D)
+        k = torch.nn.functional.linear(x, wk).view(1, L, Hkv, D)
+        v = torch.nn.functional.linear(x, wv).view(1, L, Hkv, D)
+        K.rope_qkv(q, k, v, cos, sin, kc, vc, pool_block=pool)
+
+    flush = L2Flush(dev)
+    times = {}
+    for name, fn in (("fused", fused), ("unfused", unfused), ("fused2", fused), ("unfused2", unfused)):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(args.steps):
+            flush()
+            s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            tot += s.elapsed_time(e)
+        times[name] = tot / args.steps
+    tf = min(times["fused"], times["fused2"])
+    tu = min(times["unfused"], times["unfused2"])
+    flop = 2.0 * L * N * hidden
+    burst, sustained, hbm, which = measured_peaks()
+    ach = flop / tf / 1e9
+    if rank == 0:
+        print(json.dumps({"metric": "prefill q/k/v projection + rotary + KV store TFLOP/s (single op)", "value": ach,
+                          "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": tf, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "bf16", "data": "synthetic",
+                          "config": {"workload": f"{args.workload} prefill q/k/v: L={L} hidden={hidden} Hq={Hq} "
+                                                 f"Hkv={Hkv}, pooling {'by 64' if pool else 'off'}",
+                                     "l2": L2Flush.NOTE, "fused_ms": tf, "unfused_ms": tu,
+                                     "gain_ms_per_layer": tu - tf, "runs_ms": times},
+                          "roofline": {"kernel": "sabre qkv_proj_rope_kernel", "bound": "tensor", "achieved": ach,
+                                       "peak": burst, "unit": "TFLOP/s", "frac": ach / burst,
+                                       "peak_kind": f"{which} bf16 dense, burst", "flop_per_launch": flop,
+                                       "ms_per_launch": tf, "traffic": None}}))
 
 
 def run_decode_op(args, rank, world, dist):

@@ -166,6 +166,39 @@ int sabre_rope_qkv(const void* q, const void* k, const void* v, const void* cos,
                    int dtype, void* stream);
 
 /* ------------------------------------------------------------------------
+ * (1b') Prefill q/k/v projection + rotary embedding + KV store + pooling.
+ *
+ * Replaces, for a prompt, the reference wrapper's q_proj/k_proj/v_proj,
+ * apply_rotary_pos_emb and KV-cache update
+ * (methods/sabrecoder/sabrecoder_llama_triton.py:288-299) with one kernel: a
+ * tcgen05 GEMM Y = X W^T over the concatenated bias-free weights
+ * W = [Wq; Wk; Wv] whose epilogue rounds Y to the storage dtype and then does
+ * what sabre_rope_qkv (1b) does with Y (same rounding, same pooling), so Y
+ * never goes to HBM.
+ *
+ * x        : [batch * seq_len, hidden] rows, row stride x_stride (>= hidden,
+ *            multiple of 8), 16-byte aligned
+ * w        : [(heads_q + 2 heads_kv) * 128, hidden], row-major, contiguous
+ * cos, sin : [B, L, D] strides {b, l} (b-stride 0 for one shared table)
+ * q_out    : [B, L, Hq, D] strides {b, l, h}
+ * k_out, v_out : [B, Hkv, T, D] strides {b, h, t}, T = max_seq; rows
+ *            pos0 .. pos0+L-1 are written (pos0 + L <= T)
+ * q_pool, k_pool (optional fp32 [B, Hq|Hkv, ceil(L/pool_block), D]): as in
+ *            (1b); need pool_block 64 or 128, pos0 == 0, and batch 1 or
+ *            seq_len a multiple of 256
+ * y_out    (optional): also store Y itself, [batch * seq_len, N] with row
+ *            stride y_stride (for checking the projection)
+ * head_dim must be 128; hidden a multiple of 8; strides multiples of 8
+ * elements, pointers 16-byte aligned.
+ * ---------------------------------------------------------------------- */
+int sabre_qkv_proj_rope(const void* x, const void* w, const void* cos, const void* sin, void* q_out, void* k_out,
+                        void* v_out, float* q_pool, float* k_pool, void* y_out, int batch, int seq_len, int hidden,
+                        int heads_q, int heads_kv, int head_dim, int pool_block, int pos0, int max_seq,
+                        int64_t x_stride, const int64_t* cos_strides, const int64_t* q_out_strides,
+                        const int64_t* k_out_strides, const int64_t* v_out_strides, int64_t y_stride, int dtype,
+                        void* stream);
+
+/* ------------------------------------------------------------------------
  * (1c) Decode-step q/k/v projection + rotary embedding + KV store.
  *
  * Replaces, for one new token per sequence, the reference wrapper's

@@ -34,6 +34,8 @@ SIGNATURES = {
                                          I64P, I64P, I64P, I64P, I64P, I64P, c_float, c_int, P]),
     "sabre_rope_qkv": (c_int, [P, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                c_int, I64P, I64P, I64P, I64P, I64P, I64P, I64P, c_int, P]),
+    "sabre_qkv_proj_rope": (c_int, [P, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
+                                    c_int, c_int, c_int, c_int64, I64P, I64P, I64P, I64P, c_int64, c_int, P]),
     "sabre_qkv_rope_decode": (c_int, [P, P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
                                       c_int, c_int64, c_int64, I64P, I64P, I64P, c_int, P]),
     "sabre_block_mask_workspace_size": (c_size_t, [c_int, c_int]),

@@ -98,6 +98,7 @@ static int ensure_smem_attr(Kern kern, int bytes) {
 }  // namespace sabre
 
 #include "decode_gqa.cu"
+#include "qkv_prefill.cu"
 
 using namespace sabre;
 

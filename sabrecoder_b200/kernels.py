@@ -177,6 +177,62 @@ def rope_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tenso
     return q_out, qp, kp
 
 
+def qkv_proj_rope(x: torch.Tensor, w_qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                  q_out: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor, *, pos0: int = 0,
+                  pool_block: int = 0, y_out: Optional[torch.Tensor] = None):
+    """Prefill q/k/v projection + rotary embedding + KV store (+ pooling) in
+    one kernel: ``y = x @ w_qkv.T`` rounded to the storage dtype, then as
+    :func:`rope_qkv` on y (same rounding and pooling).
+
+    x: ``[B, L, hidden]`` (unit last stride); w_qkv: ``[(Hq + 2 Hkv) * 128,
+    hidden]`` contiguous (``[Wq; Wk; Wv]``); cos, sin: ``[B or 1, >= L, 128]``;
+    q_out: ``[B, L, Hq, 128]``; k_out, v_out: ``[B, Hkv, T, 128]`` receiving
+    rows ``pos0 .. pos0+L-1``; y_out (optional): ``[B*L, N]`` gets y itself.
+    Returns ``(q_pool, k_pool)`` (None unless ``pool_block > 0``)."""
+    _need_cuda(x=x, w_qkv=w_qkv, cos=cos, sin=sin, q_out=q_out, k_out=k_out, v_out=v_out, y_out=y_out)
+    ts = (x, w_qkv, cos, sin, q_out, k_out, v_out) + ((y_out,) if y_out is not None else ())
+    if x.dtype not in DTYPE_CODE or any(t.dtype != x.dtype for t in ts):
+        raise SabreError("qkv_proj_rope: all tensors must share dtype bf16 or f16")
+    if x.dim() != 3 or x.stride(-1) != 1 or x.stride(0) != x.shape[1] * x.stride(1):
+        raise SabreError("qkv_proj_rope: x must be [B, L, hidden] with rows at one stride")
+    B, L, hidden = x.shape
+    D = q_out.shape[-1]
+    Hq = q_out.shape[2]
+    Hkv = k_out.shape[1]
+    if (q_out.dim() != 4 or tuple(q_out.shape[:2]) != (B, L) or k_out.dim() != 4 or v_out.shape != k_out.shape
+            or k_out.shape[0] != B or not w_qkv.is_contiguous()
+            or tuple(w_qkv.shape) != ((Hq + 2 * Hkv) * D, hidden)):
+        raise SabreError("qkv_proj_rope: shapes do not match x [B, L, hidden], w_qkv [(Hq+2Hkv)*D, hidden], "
+                         "q_out [B, L, Hq, D], k_out/v_out [B, Hkv, T, D]")
+    if pos0 < 0 or pos0 + L > k_out.shape[2]:
+        raise SabreError(f"qkv_proj_rope: rows {pos0}..{pos0 + L - 1} do not fit the cache of {k_out.shape[2]} rows")
+    if cos.dim() == 2:
+        cos, sin = cos.unsqueeze(0), sin.unsqueeze(0)
+    if cos.dim() != 3 or sin.shape != cos.shape or cos.shape[-1] != D or cos.shape[1] < L or cos.shape[0] not in (1, B):
+        raise SabreError(f"qkv_proj_rope: cos/sin {tuple(cos.shape)} must be [B or 1, >= L, D]")
+    if cos.stride(-1) != 1 or sin.stride() != cos.stride():
+        cos, sin = cos.contiguous(), sin.contiguous()
+    if cos.shape[0] != B:
+        cos, sin = cos.expand(B, -1, -1), sin.expand(B, -1, -1)
+    qp = kp = None
+    if pool_block > 0:
+        nb = (L + pool_block - 1) // pool_block
+        qp = torch.empty(B, Hq, nb, D, dtype=torch.float32, device=x.device)
+        kp = torch.empty(B, Hkv, nb, D, dtype=torch.float32, device=x.device)
+
+    def s3(t):
+        return i64((t.stride(0), t.stride(1), t.stride(2)))
+
+    st = lib().sabre_qkv_proj_rope(
+        x.data_ptr(), w_qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), q_out.data_ptr(), k_out.data_ptr(),
+        v_out.data_ptr(), _ptr(qp), _ptr(kp), _ptr(y_out), B, L, hidden, Hq, Hkv, D, int(pool_block), int(pos0),
+        int(k_out.shape[2]), x.stride(1), i64((cos.stride(0), cos.stride(1))), s3(q_out), s3(k_out), s3(v_out),
+        y_out.stride(0) if y_out is not None else 0, DTYPE_CODE[x.dtype], _stream(x))
+    check(st, "sabre_qkv_proj_rope")
+    LAUNCHES[0] += 1
+    return qp, kp
+
+
 def qkv_rope_decode(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, cos: torch.Tensor,
                     sin: torch.Tensor, q_out: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor,
                     pos0: int) -> torch.Tensor:

@@ -186,8 +186,10 @@ class StructureAwareAttentionWrapper(nn.Module):
                  global_last_k_chunks: int = 2, max_chunk_tokens: int = 0, use_chunk_similarity: bool = False,
                  chunk_similarity_top_percent: float = 0.1, chunk_similarity_max_tokens_per_chunk: int = 256,
                  chunk_similarity_max_neighbors: int = 8, use_crossfile_chunk_similarity: bool = False,
-                 crossfile_chunk_similarity_top_percent: Optional[float] = None, topk_blocks: int = 0):
+                 crossfile_chunk_similarity_top_percent: Optional[float] = None, topk_blocks: int = 0,
+                 fused_prefill_projection: bool = False):
         super().__init__()
+        self.fused_prefill_projection = bool(fused_prefill_projection)
         self.original_attn = original_attn
         self.tokenizer = tokenizer
         self.use_sparse_for_generation = use_sparse_for_generation
@@ -245,6 +247,44 @@ class StructureAwareAttentionWrapper(nn.Module):
             return False
         return hidden_states.data_ptr() % 16 == 0 and all(m.weight.data_ptr() % 16 == 0 for m in projs)
 
+    def _fused_prefill_ok(self, hidden_states: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                          pooling: bool) -> bool:
+        """Whether a prompt can use the fused projection + rotary + KV-store
+        GEMM (sabre_qkv_proj_rope): opted in, plain bias-free projections of
+        the activations' dtype, 128-wide heads, and, when pooling, one
+        sequence or a length that is a multiple of 256."""
+        if not self.fused_prefill_projection:
+            return False
+        projs = (self.q_proj, self.k_proj, self.v_proj)
+        if any(not isinstance(m, nn.Linear) or m.bias is not None for m in projs):
+            return False
+        dt = hidden_states.dtype
+        if dt not in (torch.bfloat16, torch.float16) or not hidden_states.is_cuda or self.head_dim != 128:
+            return False
+        if any(m.weight.dtype != dt or m.weight.device != hidden_states.device for m in projs):
+            return False
+        B, L, hidden = hidden_states.shape
+        if hidden % 8 or not hidden_states.is_contiguous() or hidden_states.data_ptr() % 16:
+            return False
+        if cos.dtype != dt or sin.shape != cos.shape or cos.shape[-1] != 128:
+            return False
+        return not pooling or B == 1 or L % 256 == 0
+
+    def _qkv_weight(self) -> torch.Tensor:
+        """[Wq; Wk; Wv] as one contiguous tensor. Made once: the three
+        projections' weights then become views of it, so no weight memory is
+        duplicated and the decode path keeps reading the same values."""
+        w = getattr(self, "_w_qkv", None)
+        if w is None or w.data_ptr() != self.q_proj.weight.data_ptr():
+            with torch.no_grad():
+                w = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight]).contiguous()
+                nq, nk = self.q_proj.weight.shape[0], self.k_proj.weight.shape[0]
+                self.q_proj.weight.data = w[:nq]
+                self.k_proj.weight.data = w[nq:nq + nk]
+                self.v_proj.weight.data = w[nq + nk:]
+            self._w_qkv = w
+        return w
+
     def forward(self, hidden_states: torch.Tensor, position_embeddings: Tuple[torch.Tensor, torch.Tensor] = None,
                 attention_mask: Optional[torch.Tensor] = None, past_key_value=None,
                 cache_position: Optional[torch.LongTensor] = None, past_key_values=None, **kwargs):
@@ -265,6 +305,20 @@ class StructureAwareAttentionWrapper(nn.Module):
             def store(k_out, v_out, pos):
                 K.qkv_rope_decode(hidden_states.view(B, -1), *w, cos.reshape(B, D), sin.reshape(B, D),
                                   q.view(B, Hq, D), k_out, v_out, pos)
+        elif L > 1 and self._fused_prefill_ok(hidden_states, cos, sin,
+                                              pooling=self.sparse_attn.topk_blocks > 0):
+            # A prompt: one GEMM for the three projections whose epilogue
+            # rotates q and k, stores K and V and pools the blocks.
+            w_qkv = self._qkv_weight()
+            Hq = self.q_proj.weight.shape[0] // D
+            Hkv = self.k_proj.weight.shape[0] // D
+            q = torch.empty(B, L, Hq, D, dtype=hidden_states.dtype, device=hidden_states.device)
+            pool_block = self.block_size if self.sparse_attn.topk_blocks > 0 else 0
+
+            def store(k_out, v_out, pos):
+                nonlocal qp, kp
+                qp, kp = K.qkv_proj_rope(hidden_states, w_qkv, cos, sin, q, k_out, v_out, pos0=pos,
+                                         pool_block=pool_block if pos == 0 else 0)
         else:
             q = self.q_proj(hidden_states).view(B, L, -1, D)
             k = self.k_proj(hidden_states).view(B, L, -1, D)
@@ -348,8 +402,15 @@ def patch_model_with_sabrecoder_attention(model, tokenizer, use_sparse_for_gener
                                           chunk_similarity_max_neighbors: int = 8,
                                           use_crossfile_chunk_similarity: bool = False,
                                           crossfile_chunk_similarity_top_percent: Optional[float] = None,
-                                          topk_blocks: int = 0, verbose: bool = True):
-    """Replace every ``layer.self_attn`` with the wrapper (reference :322-402)."""
+                                          topk_blocks: int = 0, fused_prefill_projection: bool = False,
+                                          verbose: bool = True):
+    """Replace every ``layer.self_attn`` with the wrapper (reference :322-402).
+
+    ``fused_prefill_projection=True`` runs each prompt's q/k/v projections,
+    rotary embedding, KV store and block pooling as one GEMM kernel
+    (sabre_qkv_proj_rope) instead of three cuBLAS projections followed by the
+    fused RoPE/KV kernel; the results agree to the GEMMs' accumulation order
+    (RoPE itself is bit-exact on either path)."""
     if verbose:
         mode = "Full Sparse" if use_sparse_for_generation else "Hybrid (Sparse Prefill, Dense Generation)"
         print(f"Applying SabreCoder B200 attention [{mode}] block={block_size} window={window_size} "
@@ -373,7 +434,7 @@ def patch_model_with_sabrecoder_attention(model, tokenizer, use_sparse_for_gener
                 chunk_similarity_max_neighbors=chunk_similarity_max_neighbors,
                 use_crossfile_chunk_similarity=use_crossfile_chunk_similarity,
                 crossfile_chunk_similarity_top_percent=crossfile_chunk_similarity_top_percent,
-                topk_blocks=topk_blocks)
+                topk_blocks=topk_blocks, fused_prefill_projection=fused_prefill_projection)
             count += 1
     if verbose:
         print(f"Replaced {count} attention layers with block-sparse B200 attention")
@@ -388,7 +449,7 @@ def patch_model_with_sabrecoder_attention(model, tokenizer, use_sparse_for_gener
         "chunk_similarity_max_neighbors": chunk_similarity_max_neighbors,
         "use_crossfile_chunk_similarity": use_crossfile_chunk_similarity,
         "crossfile_chunk_similarity_top_percent": crossfile_chunk_similarity_top_percent,
-        "topk_blocks": topk_blocks,
+        "topk_blocks": topk_blocks, "fused_prefill_projection": fused_prefill_projection,
     }
     return model
 

@@ -135,3 +135,22 @@ def test_kernel_calls_fail_loudly_without_cuda_tensors():
     q = torch.zeros(1, 1, 64, 128, dtype=torch.bfloat16)
     with pytest.raises(_lib.SabreError, match="CUDA tensor"):
         kernels.prefill_bsa(q, q, q, torch.zeros(1, 1, 1, dtype=torch.int32), torch.ones(1, 1, dtype=torch.int32), 64)
+
+
+def test_qkv_proj_rope_rejects_bad_arguments_before_launch():
+    L = _lib.lib()
+    st = _lib.i64([1024, 128, 128])
+
+    def call(seq_len=256, pos0=0, max_seq=512, pool=None, pool_block=64, batch=1, hidden=2048, xs=2048):
+        return L.sabre_qkv_proj_rope(16, 16, 16, 16, 16, 16, 16, pool, None, None, batch, seq_len, hidden, 2, 2,
+                                     128, pool_block, pos0, max_seq, xs, st, st, st, st, 0, 0, None)
+
+    assert call(seq_len=600) == -1 and b"outside the cache" in L.sabre_last_error()
+    assert call(pos0=-1) == -1
+    assert call(hidden=2044, xs=2044) == -3
+    assert call(xs=1024) == -3
+    assert call(pool=16, pool_block=32) == -2 and b"pooling" in L.sabre_last_error()
+    assert call(pool=16, pos0=4) == -2
+    assert call(pool=16, batch=2, seq_len=200) == -2
+    assert L.sabre_qkv_proj_rope(None, 16, 16, 16, 16, 16, 16, None, None, None, 1, 4, 256, 2, 2, 128, 0, 0, 8, 256,
+                                 st, st, st, st, 0, 0, None) == -1

@@ -446,3 +446,53 @@ def test_attention_module_token_level_end_to_end(cuda):
     ref = AO.token_masked_prefill_fp32(q, k, v, vis)
     err = (out.float().cpu() - ref).abs()
     assert err.max().item() < 2e-2 and err.mean().item() < 2e-3
+
+
+@pytest.mark.parametrize("topk", [0, 8])
+def test_fused_prefill_projection_matches_the_unfused_path(cuda, topk):
+    """fused_prefill_projection=True (one GEMM whose epilogue does RoPE, the
+    KV store and pooling) against the default path (cuBLAS projections, then
+    the RoPE/KV kernel) on the same bf16 model and prompt: the projections
+    differ only in GEMM accumulation order, so the prefill logits and the
+    cached K/V agree to bf16 rounding."""
+    import copy
+
+    from sabrecoder_b200 import sabrecoder_llama as SL
+    from sabrecoder_b200.kv_cache import SabreKVCache
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+    from sabrecoder_b200.spans import make_spans
+    L, block = 700, 64
+    base = _tiny_llama(4, 2).to(cuda)
+    mk = dict(block_size=block, window_size=192, num_prefix_tokens=64, num_suffix_tokens=128,
+              global_last_k_chunks=0, max_chunk_tokens=128)
+    models = []
+    for fused in (False, True):
+        m = copy.deepcopy(base)
+        SL.patch_model_with_sabrecoder_attention(m, None, topk_blocks=topk, fused_prefill_projection=fused,
+                                                 verbose=False, **mk)
+        models.append(m)
+    mb = StructureAwareMaskBuilder(None, **mk)
+    bi, bc, bm = mb.build_block_indices_from_spans(make_spans(L, 8), cuda)
+    ids = torch.randint(0, 512, (1, L), generator=torch.Generator().manual_seed(1)).to(cuda)
+    SL.set_current_code("<prompt>")
+    SL.set_precomputed_blocks(bi, bc)
+    outs, caches = [], []
+    try:
+        with torch.no_grad():
+            for m in models:
+                c = SabreKVCache(m.config, batch_size=1, max_cache_len=L + 8, device=cuda)
+                outs.append(m(input_ids=ids, past_key_values=c, use_cache=True).logits.float())
+                caches.append(c)
+    finally:
+        SL.clear_current_code()
+        SL.clear_precomputed_blocks()
+    a, b = outs
+    scale = b.abs().max().item()
+    assert (a - b).abs().max().item() <= 3e-2 * scale
+    for la, lb in zip(caches[0].layers, caches[1].layers):
+        for ta, tb in ((la.keys, lb.keys), (la.values, lb.values)):
+            assert (ta.float() - tb.float()).abs().max().item() <= 2e-2 * tb.float().abs().max().item()
+    # the fused path really ran: the three projections became views of one weight
+    attn = models[1].model.layers[0].self_attn
+    assert getattr(attn, "_w_qkv", None) is not None
+    assert attn.k_proj.weight.data_ptr() == attn._w_qkv.data_ptr() + attn.q_proj.weight.numel() * 2

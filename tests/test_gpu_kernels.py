@@ -426,3 +426,85 @@ def test_rope_qkv_bit_exact_with_hf(K, B, L, Hq, Hkv, pool, dtype):
     if pool:
         np.testing.assert_array_equal(qp.cpu().numpy(), MO.pooled_block_means(rq.float().numpy(), L, pool))
         np.testing.assert_array_equal(kp.cpu().numpy(), MO.pooled_block_means(rk.float().numpy(), L, pool))
+
+
+# (B, L, hidden, Hq, Hkv, pool_block, pos0, dtype): partial M and N tiles (7 + 2 heads = 4.5 tiles of
+# 256 columns), sequences straddling 256-row tiles (B=2, L=200), pooling by 64 and 128, a cache offset.
+@pytest.mark.parametrize("B,L,hidden,Hq,Hkv,pool,pos0,dtype", [
+    (1, 1000, 512, 4, 2, 64, 0, torch.bfloat16),
+    (2, 512, 256, 2, 2, 64, 0, torch.bfloat16),
+    (1, 300, 1024, 7, 1, 128, 0, torch.bfloat16),
+    (2, 200, 256, 2, 1, 0, 5, torch.bfloat16),
+    (1, 257, 384, 2, 2, 64, 0, torch.float16),
+])
+def test_qkv_proj_rope_matches_projection_and_hf_rope(K, B, L, hidden, Hq, Hkv, pool, pos0, dtype):
+    """Fused prefill projection: y = x W^T within bf16/fp16 rounding of an
+    fp32 product; q/k rotated bit-exactly as apply_rotary_pos_emb rotates the
+    kernel's own y; v stored as y; pools equal the oracle's block means of
+    the rotated rows; cache rows outside pos0 .. pos0+L-1 untouched."""
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+    gen = torch.Generator().manual_seed(L + hidden + Hq)
+    D = 128
+    N = (Hq + 2 * Hkv) * D
+    x = (torch.randn(B, L, hidden, generator=gen) * 0.5).to(dtype)
+    w = (torch.randn(N, hidden, generator=gen) / hidden ** 0.5).to(dtype)
+    ang = torch.rand(B, L, D // 2, generator=gen) * 50
+    emb = torch.cat([ang, ang], -1)
+    cos, sin = emb.cos().to(dtype), emb.sin().to(dtype)
+    T = pos0 + L + 3
+    sentinel = torch.full((B, Hkv, T, D), 7.0, dtype=dtype)
+    kc, vc = sentinel.clone().cuda(), sentinel.clone().cuda()
+    q_out = torch.empty(B, L, Hq, D, dtype=dtype, device="cuda")
+    y = torch.empty(B * L, N, dtype=dtype, device="cuda")
+    qp, kp = K.qkv_proj_rope(x.cuda(), w.cuda(), cos.cuda(), sin.cuda(), q_out, kc, vc, pos0=pos0, pool_block=pool,
+                             y_out=y)
+    torch.cuda.synchronize()
+    ref = (x.float().reshape(B * L, hidden) @ w.float().T)
+    yc = y.float().cpu()
+    assert (yc - ref).abs().max().item() <= 8e-3 * ref.abs().max().item()
+    assert (yc - ref).abs().mean().item() <= 2e-3 * ref.abs().mean().item() + 1e-6
+    yv = y.cpu().view(B, L, Hq + 2 * Hkv, D)
+    q, k, v = yv[:, :, :Hq], yv[:, :, Hq:Hq + Hkv], yv[:, :, Hq + Hkv:]
+    rq, rk = apply_rotary_pos_emb(q.transpose(1, 2), k.transpose(1, 2), cos, sin)
+    assert torch.equal(q_out.cpu().transpose(1, 2), rq)
+    assert torch.equal(kc[:, :, pos0:pos0 + L].cpu(), rk)
+    assert torch.equal(vc[:, :, pos0:pos0 + L].cpu(), v.transpose(1, 2))
+    outside = torch.ones(T, dtype=torch.bool)
+    outside[pos0:pos0 + L] = False
+    assert torch.equal(kc[:, :, outside].cpu(), sentinel[:, :, outside])
+    assert torch.equal(vc[:, :, outside].cpu(), sentinel[:, :, outside])
+    if pool:
+        np.testing.assert_array_equal(qp.cpu().numpy(), MO.pooled_block_means(rq.float().numpy(), L, pool))
+        np.testing.assert_array_equal(kp.cpu().numpy(), MO.pooled_block_means(rk.float().numpy(), L, pool))
+    assert K.device_status(clear=True) == 0
+
+
+def test_qkv_proj_rope_at_the_1p3b_layer_shape(K):
+    """One c1 layer: 12288 tokens, hidden 2048, 16 + 16 + 16 heads, pooled by 64."""
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    B, L, hidden, Hq, Hkv, D = 1, 12288, 2048, 16, 16, 128
+    N = (Hq + 2 * Hkv) * D
+    x = (torch.randn(B, L, hidden, generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, hidden, generator=gen, device="cuda") / hidden ** 0.5).to(torch.bfloat16)
+    ang = torch.rand(1, L, D // 2, generator=gen, device="cuda") * 50
+    emb = torch.cat([ang, ang], -1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    kc = torch.zeros(B, Hkv, L + 64, D, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    q_out = torch.empty(B, L, Hq, D, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(B * L, N, dtype=torch.bfloat16, device="cuda")
+    qp, kp = K.qkv_proj_rope(x, w, cos, sin, q_out, kc, vc, pool_block=64, y_out=y)
+    ref = torch.nn.functional.linear(x, w).view(B * L, N)  # cuBLAS, bf16 out
+    torch.cuda.synchronize()
+    d = (y.float() - ref.float()).abs()
+    assert d.max().item() <= 8e-3 * ref.float().abs().max().item()
+    yv = y.view(B, L, Hq + 2 * Hkv, D)
+    rq, rk = apply_rotary_pos_emb(yv[:, :, :Hq].transpose(1, 2), yv[:, :, Hq:Hq + Hkv].transpose(1, 2), cos, sin)
+    assert torch.equal(q_out.transpose(1, 2), rq)
+    assert torch.equal(kc[:, :, :L], rk)
+    assert torch.equal(vc[:, :, :L], yv[:, :, Hq + Hkv:].transpose(1, 2))
+    for h in (0, Hq - 1):
+        np.testing.assert_array_equal(qp[:, h:h + 1].cpu().numpy(),
+                                      MO.pooled_block_means(rq[:, h:h + 1].float().cpu().numpy(), L, 64))
+    assert K.device_status(clear=True) == 0
