@@ -739,16 +739,16 @@ class StructureAwareMaskBuilder:
     def _structure_backends(self):
         """Segmenter and analyser classes: the ones passed to the constructor,
         else the reference's tree-sitter modules when importable, else the
-        built-in Python ones (:mod:`sabrecoder_b200.structure`, Python source
-        only; other languages raise there)."""
+        built-in ones: Python on the ``ast`` tree (:mod:`sabrecoder_b200.structure`),
+        Java and C# on a token stream (:mod:`sabrecoder_b200.structure_braces`)."""
         seg, ana = self.segmenter_factory, self.analyzer_factory
         if seg is None or ana is None:
             try:
                 from semantic_chunker import TreeSitterSegmenter  # the reference's segmenter, if importable
                 from reference_graph import CrossReferenceAnalyzer
             except Exception:  # noqa: BLE001  (tree-sitter not installed)
-                from .structure import PythonReferenceAnalyzer as CrossReferenceAnalyzer
-                from .structure import PythonSegmenter as TreeSitterSegmenter
+                from .structure_braces import StructureAnalyzer as CrossReferenceAnalyzer
+                from .structure_braces import StructureSegmenter as TreeSitterSegmenter
             seg = seg or TreeSitterSegmenter
             ana = ana or CrossReferenceAnalyzer
         return seg, ana

@@ -66,6 +66,31 @@ def test_build_block_indices_with_segmenter_bit_exact(cuda):
     np.testing.assert_array_equal(bc.cpu().numpy(), g["block_counts"])
 
 
+@pytest.mark.parametrize("lang", ["java", "c_sharp"])
+def test_build_block_indices_java_csharp_without_tree_sitter(cuda, lang):
+    """Java / C# prompts through the built-in token-stream segmenter and
+    analyser: the GPU mask and lists equal the oracle's for the same chunks
+    and edges."""
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder, clear_all_caches
+    from sabrecoder_b200.spans import LineTokenizer
+    from test_structure_braces import synthetic_source
+    code, _ = synthetic_source(lang)
+    L = len(code.split("\n"))
+    kw = dict(block_size=4, window_size=4, num_prefix_tokens=4, num_suffix_tokens=8, global_last_k_chunks=1)
+    clear_all_caches()
+    mb = StructureAwareMaskBuilder(LineTokenizer(), **kw)
+    bi, bc, bm = mb.build_block_indices(code, L, cuda, language=lang)
+    st = mb._structure_for_code(code, lang)
+    assert len(st["chunks"]) > 120 and st["chunk_deps"]
+    want = MO.build_block_mask_from_chunks(code=code, seq_len=L, chunks=st["chunks"], chunk_deps=st["chunk_deps"],
+                                           import_chunks=st["import_chunks"], language=lang,
+                                           tokenizer=LineTokenizer(), max_chunk_tokens=0, **kw)
+    np.testing.assert_array_equal(bm.cpu().numpy(), want)
+    ri, rc = MO.block_indices_from_mask(np.asarray(want)[None])
+    np.testing.assert_array_equal(bc.cpu().numpy(), rc)
+    np.testing.assert_array_equal(bi.cpu().numpy()[..., :ri.shape[-1]], ri)
+
+
 def test_compute_block_indices_from_mask(cuda):
     from sabrecoder_b200.sabrecoder_attention import compute_block_indices_from_mask
     g = G.load("mask_c3_16384.npz")
