@@ -505,7 +505,7 @@ def run_ours(args, rank, world, dist):
     # flushed, so every bench line carries a 16K roofline.
     roof16 = None
     if not args.no_op16k:
-        ms16, flop16, dens16, H16, L16 = op_measure("c3", rank, max(3, min(args.steps, 10)), 3)
+        ms16, flop16, dens16, H16, L16, iss16 = op_measure("c3", rank, max(3, min(args.steps, 10)), 3)
         ach16 = flop16 / ms16 / 1e9
         roof16 = {"kernel": "sabre prefill_bsa_kernel", "bound": "tensor",
                   "workload": f"attention op B=1 H={H16} L={L16} D=128 block 64, structure + top-{TOPK}, "
@@ -513,6 +513,7 @@ def run_ours(args, rank, world, dist):
                   "achieved": ach16, "peak": burst, "unit": "TFLOP/s", "frac": ach16 / burst,
                   "peak_kind": f"{which} bf16 dense, burst (kernel timed alone)",
                   "frac_of_sustained": ach16 / sustained, "flop_per_launch": flop16, "ms_per_launch": ms16,
+                  "issued_flop_per_launch": iss16, "issued_tflops": iss16 / ms16 / 1e9,
                   "traffic": profile_traffic("prefill_bsa_c3_op")}
 
     weight_gb = sum(p.numel() * p.element_size() for p in model.parameters()) / 1e9
@@ -632,12 +633,30 @@ OP_SHAPES = {"c0": (16, 4096, "spans"), "c1": (16, 12288, "bench"), "c2": (16, 1
              "c3": (32, 16384, "bench")}
 
 
+def issued_tile_flop(idx, cnt) -> float:
+    """MMA work the prefill kernel issues for block-64 lists: a 128-row CTA
+    runs S = Q K^T and P V over the union of its two 64-row query blocks'
+    key tiles (listed, and not after the block), 4 x 128 x 64 x 128 FLOP per
+    tile; the algorithmic count takes each block's own list only."""
+    import torch
+    _, H, nb, ma = idx.shape
+    dev = idx.device
+    pos = torch.arange(ma, device=dev).view(1, 1, ma)
+    qb = torch.arange(nb, device=dev).view(1, nb, 1)
+    kb = idx[0].long()
+    valid = (pos < cnt[0].unsqueeze(-1)) & (kb >= 0) & (kb <= qb)
+    m = torch.zeros(H, nb + (nb & 1), nb + 1, dtype=torch.bool, device=dev)
+    m[:, :nb].scatter_(2, torch.where(valid, kb, torch.full_like(kb, nb)), True)
+    tiles = m[..., :nb].view(H, -1, 2, nb).any(2).sum().item()
+    return float(tiles) * 4 * 128 * 64 * 128
+
+
 def op_measure(name: str, rank: int, steps: int, warmup: int):
     """The prefill attention op alone on one layer's shape of a workload
     (c0: B=1, H=16, L=4096; c1: H=16, L=12288; c3: H=32, L=16384), block 64,
     structure + pooled top-8 lists, L2 flushed between timed launches (the
     flush is outside the timed window). Returns (ms per launch, algorithmic
-    FLOP per launch, density, H, L)."""
+    FLOP per launch, density, H, L, issued FLOP per launch)."""
     import torch
     from sabrecoder_b200 import kernels as K
     from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
@@ -673,12 +692,12 @@ def op_measure(name: str, rank: int, steps: int, warmup: int):
     flop = float(cnt.sum().item()) * 4 * blk * blk * 128
     nb = bm.shape[0]
     dens = float(cnt.sum().item()) / (H * nb * (nb + 1) / 2)
-    return ms, flop, dens, H, L
+    return ms, flop, dens, H, L, issued_tile_flop(idx, cnt)
 
 
 def run_op_bench(args, rank, world, dist):
     """The prefill attention op alone on one layer's shape of the workload."""
-    ms, flop, dens, H, L = op_measure(args.workload, rank, args.steps, args.warmup)
+    ms, flop, dens, H, L, issued = op_measure(args.workload, rank, args.steps, args.warmup)
     burst, sustained, hbm, which = measured_peaks()
     traffic = profile_traffic(f"prefill_bsa_{args.workload}_op")
     if rank == 0:
@@ -692,7 +711,9 @@ def run_op_bench(args, rank, world, dist):
                           "roofline": {"kernel": "sabre prefill_bsa_kernel", "bound": "tensor",
                                        "achieved": flop / ms / 1e9, "peak": burst, "unit": "TFLOP/s",
                                        "frac": flop / ms / 1e9 / burst, "peak_kind": f"{which} bf16 dense, burst",
-                                       "flop_per_launch": flop, "ms_per_launch": ms, "traffic": traffic}}))
+                                       "flop_per_launch": flop, "ms_per_launch": ms,
+                                       "issued_flop_per_launch": issued, "issued_tflops": issued / ms / 1e9,
+                                       "traffic": traffic}}))
 
 
 def _events_ms(fn, steps, warmup):

@@ -351,39 +351,53 @@ __global__ void __launch_bounds__(kThreads, 2)
         tw = (vis && rank < tcount) ? p.tmask[(tbase + rank) * 64 + (row & 63)] : 0ull;
         rank += vis ? 1 : 0;
       }
+      const int nvalid = vis ? min(64, max(0, r_abs - kt * 64 + 1)) : 0;
+      // A warp whose 32 rows see no key of this tile (the tile is listed
+      // only by the other half, or lies wholly after the rows) stores P = 0
+      // and leaves the exponential unit to the other warps of its SM
+      // sub-partition.
+      const bool dead = __all_sync(0xffffffffu, nvalid == 0);
       ok = mbar_wait_warp(bar(S_FULL + j % kKStages), (j / kKStages) & 1, abort_flag);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr0[32], sr1[32];
-      tmem_ld32(tl + kTmemS, sr0);
-      tmem_ld32(tl + kTmemS + 32, sr1);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(S_EMPTY));
-
-      const int nvalid = vis ? min(64, max(0, r_abs - kt * 64 + 1)) : 0;
-      float x[64];
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        x[c] = __uint_as_float(sr0[c]);
-        x[c + 32] = __uint_as_float(sr1[c]);
-      }
-      if (nvalid < 64 || (kTok && tw != ~0ull)) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (c >= nvalid || !((tw >> c) & 1ull)) x[c] = -INFINITY;
-      }
-      const float mx = row_max64(x);
-      const float m_tile = mx * sl2;
-      const bool rescale = m_tile > m_run + 8.0f;
-      const float m_use = rescale ? m_tile : m_run;
-      const float alpha = rescale ? ex2(m_run - m_use) : 1.0f;
-      const float moff = (m_use == -INFINITY) ? 0.0f : m_use;
       uint32_t pk[32];
-      const float rs = exp_tile<T>(x, sl2, moff, pk);
-      l_run = l_run * alpha + rs;
-      m_run = m_use;
+      bool rescale = false;
+      float alpha = 1.0f;
+      if (dead) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(S_EMPTY));
+#pragma unroll
+        for (int c = 0; c < 32; ++c) pk[c] = 0u;
+      } else {
+        uint32_t sr0[32], sr1[32];
+        tmem_ld32(tl + kTmemS, sr0);
+        tmem_ld32(tl + kTmemS + 32, sr1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(S_EMPTY));
+        float x[64];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          x[c] = __uint_as_float(sr0[c]);
+          x[c + 32] = __uint_as_float(sr1[c]);
+        }
+        if (nvalid < 64 || (kTok && tw != ~0ull)) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (c >= nvalid || !((tw >> c) & 1ull)) x[c] = -INFINITY;
+        }
+        const float mx = row_max64(x);
+        const float m_tile = mx * sl2;
+        rescale = m_tile > m_run + 8.0f;
+        const float m_use = rescale ? m_tile : m_run;
+        alpha = rescale ? ex2(m_run - m_use) : 1.0f;
+        const float moff = (m_use == -INFINITY) ? 0.0f : m_use;
+        const float rs = exp_tile<T>(x, sl2, moff, pk);
+        l_run = l_run * alpha + rs;
+        m_run = m_use;
+      }
 
       // O must not change under a running P.V: rescale only after P.V(j-1).
       if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
