@@ -69,6 +69,9 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8], bool bf16
 template <typename T, int G>
 __global__ void __launch_bounds__(kThreads) decode_split_kernel(const Params p) {
   constexpr bool kBf16 = DT<T>::kBf16;
+  // Let the combine kernel (a programmatic dependent launch) become resident
+  // now: its griddepcontrol.wait still waits for this whole grid.
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int split = blockIdx.x;
   const int hk = blockIdx.y;
   const int b = blockIdx.z;
@@ -250,6 +253,13 @@ struct ChunkWalk {
       : ip(ip_), sk(sk_), jj(j0 - 1), j1(j1_), block(block_), T_valid(T_valid_), kb(0), sub(0) {
     sub = block_ / kChunkRows;  // forces a fetch on the first next()
   }
+  // Starts the walk at entry j0 with its value already read (j0 < j1).
+  __device__ void seed(int kb0) {
+    if (jj + 1 >= j1) return;
+    jj += 1;
+    kb = kb0;
+    sub = (kb < 0) ? block / kChunkRows : 0;
+  }
   // Next chunk: first row t0 and valid rows; false when the share is exhausted.
   __device__ bool next(long long& t0, int& rows) {
     for (;;) {
@@ -274,6 +284,9 @@ struct ChunkWalk {
 template <typename T, int G>
 __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Params p) {
   constexpr bool kBf16 = DT<T>::kBf16;
+  // Let the combine kernel (a programmatic dependent launch) become resident
+  // now: its griddepcontrol.wait still waits for this whole grid.
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   const int split = blockIdx.x;
@@ -288,6 +301,13 @@ __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Para
   auto full_bar = [&](int s) -> uint32_t { return sbase + kBulkBarOff + 8u * s; };
   auto empty_bar = [&](int s) -> uint32_t { return sbase + kBulkBarOff + 8u * (kBulkStages + s); };
 
+  // The sequence length, the list count and the split's first index are
+  // independent loads, issued together before the barrier set-up.
+  const int T_valid = min(p.seq_lens[b], p.Tmax);
+  int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];
+  const int j0 = split * p.bps;
+  const int32_t* ip = p.idx + b * p.idx_sb + hk * p.idx_sh;
+  const int first_kb = (warp == kBulkConsumerWarps && lane == 0 && j0 < p.max_active) ? ip[j0 * p.idx_sk] : -1;
   if (tid == 0) {
     *abort_flag = 0;
     for (int s = 0; s < kBulkStages; ++s) {
@@ -297,13 +317,8 @@ __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Para
     fence_mbar_init();
   }
   __syncthreads();
-
-  const int T_valid = min(p.seq_lens[b], p.Tmax);
-  int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];
   cnt = min(cnt, p.max_active);
-  const int j0 = split * p.bps;
   const int j1 = min(j0 + p.bps, cnt);
-  const int32_t* ip = p.idx + b * p.idx_sb + hk * p.idx_sh;
   const T* kbase = static_cast<const T*>(p.kc) + b * p.k_sb + hk * p.k_sh;
   const T* vbase = static_cast<const T*>(p.vc) + b * p.v_sb + hk * p.v_sh;
 
@@ -312,6 +327,7 @@ __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Para
     // ---------------- producer ----------------
     if (lane == 0) {
       ChunkWalk walk(ip, p.idx_sk, j0, j1, p.block, T_valid);
+      walk.seed(first_kb);
       long long t0;
       int rows;
       int issued[kBulkStages] = {0, 0, 0};

@@ -58,6 +58,9 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
     decode_gqa_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       const Params p) {
+  // Let the combine kernel (a programmatic dependent launch) become resident
+  // now: its griddepcontrol.wait still waits for this whole grid.
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
