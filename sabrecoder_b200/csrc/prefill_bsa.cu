@@ -12,16 +12,20 @@
 //              soon as the S = Q K^T that read it completes)
 //   warp 5     TMEM allocator and single-thread tcgen05.mma issuer
 //   warp 6     TMA producer for V (2-stage ring, released when P.V completes)
-// Each tcgen05.commit costs the tensor pipe about as much as a small MMA, so
-// a key tile takes two: S_FULL[stage] after its S = Q K^T (read by the
-// softmax, and by the K producer as "stage free"), and P_EMPTY[buffer] after
-// its P.V (read by the softmax, and by the V producer: V stage i%2 and P
-// buffer i%2 are released by the same P.V). Each barrier's next completion
-// needs its waiter's own next step, so no waiter can miss a phase.
-// TMEM (256 columns): O [0,128), S [128,192), P0 [192,224), P1 [224,256).
+// Two S buffers, with P written over its own S: S(j+1) is issued right after
+// P.V(j-1) (which read P(j-1) from the columns S(j+1) overwrites; the tensor
+// pipe runs a thread's MMAs in issue order), so it is computed while the
+// softmax works on S(j), and the softmax never waits for a P buffer.
+// Commits per key tile: K_FREE[stage] and S_FULL[buffer] after S = Q K^T
+// (the K producer's "stage free" and the softmax's "S ready"), PV_DONE[buffer]
+// after P.V (the V producer's "stage free", and the softmax's wait before it
+// rescales O). Each barrier's next completion needs its waiter's own next
+// step, so no waiter can miss a phase.
+// TMEM (256 columns): O [0,128), S0 [128,192), S1 [192,256); P(j) (bf16
+// pairs) over the first 32 columns of S(j%2).
 //   S = Q K^T      M=128 N=64  K=128, A and B from shared memory
-//   O += P V       M=128 N=128 K=64,  A (P, bf16 pairs) from TMEM, B (V)
-//                  from shared memory (MN-major)
+//   O += P V       M=128 N=128 K=64,  A (P) from TMEM, B (V) from shared
+//                  memory (MN-major)
 // Shared memory (bytes): Q 32768 | K 3x16384 | V 2x16384 | key-tile bitmaps
 // 256 | barriers (~112.5 KB).
 // A CTA's fixed costs are kept off its critical path: the Q tile is
@@ -62,22 +66,22 @@ constexpr int kKOff = kQOff + kQBytes;
 constexpr int kVOff = kKOff + kKStages * kKVStageBytes;
 constexpr int kBitsOff = kVOff + kVStages * kKVStageBytes;
 constexpr int kBarOff = kBitsOff + 2 * kWords * 4;
+static_assert(kVStages == 2, "V stage j%2 is released with S buffer j%2");
 enum Bar {
   Q_FULL = 0,
-  K_FULL = 1,                     // [3]
+  K_FULL = 1,                     // [kKStages]
   V_FULL = K_FULL + kKStages,     // [2]
-  S_FULL = V_FULL + kVStages,     // [3] one per K stage; also "K stage free"
-  S_EMPTY = S_FULL + kKStages,
-  P_FULL = S_EMPTY + 1,           // [2]
-  P_EMPTY = P_FULL + 2,           // [2]
-  MMA_DONE = P_EMPTY + 2,
+  K_FREE = V_FULL + kVStages,     // [kKStages] S(j) done: K stage j%kKStages free
+  S_FULL = K_FREE + kKStages,     // [2] S(j) done in S buffer j%2
+  P_FULL = S_FULL + 2,            // [2] P(j) stored over S buffer j%2 (one arrival per softmax warp)
+  PV_DONE = P_FULL + 2,           // [2] P.V(j) done: V stage j%2 free
+  MMA_DONE = PV_DONE + 2,
   NUM_BARS = MMA_DONE + 1
 };
 constexpr int kMiscOff = kBarOff + NUM_BARS * 8;
 constexpr int kSmemBytes = kMiscOff + 16;
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kTmemS = 128;
-constexpr uint32_t kTmemP = 192;  // + 32 * buffer
+constexpr uint32_t kTmemS = 128;  // + 64 * buffer: S(j) fp32, then P(j) (bf16 pairs) over its first 32 columns
 
 struct Params {
   // Token-level variant only (block size 64): the 64-bit row masks of every
@@ -191,13 +195,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(bar(Q_FULL), 1);
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(bar(K_FULL + s), 1);
-      mbar_init(bar(S_FULL + s), 1);
+      mbar_init(bar(K_FREE + s), 1);
     }
-    for (int s = 0; s < kVStages; ++s) mbar_init(bar(V_FULL + s), 1);
-    mbar_init(bar(S_EMPTY), 4);  // one arrival per softmax warp
     for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(V_FULL + s), 1);
+      mbar_init(bar(S_FULL + s), 1);
       mbar_init(bar(P_FULL + s), 4);
-      mbar_init(bar(P_EMPTY + s), 1);
+      mbar_init(bar(PV_DONE + s), 1);
     }
     mbar_init(bar(MMA_DONE), 1);
     fence_mbar_init();
@@ -254,8 +258,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool is_k = (warp == 4);
       const int stages = is_k ? kKStages : kVStages;
       const int full0 = is_k ? K_FULL : V_FULL;
-      // K stage s is free when S_FULL[s] completes, V stage s when P_EMPTY[s] does.
-      const int empty0 = is_k ? S_FULL : P_EMPTY;
+      // K stage s is free when K_FREE[s] completes, V stage s when PV_DONE[s] does.
+      const int empty0 = is_k ? K_FREE : PV_DONE;
       const uint32_t ring = sbase + (is_k ? kKOff : kVOff);
       const CUtensorMap* map = is_k ? &tmK : &tmV;
       int issued[kKStages] = {0, 0, 0};
@@ -287,37 +291,43 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t kd0 = smem_desc_sw128(sbase + kKOff, 16, 1024);
       const uint64_t vd0 = smem_desc_sw128(sbase + kVOff, kKVStageBytes / 2, 1024);
       const uint32_t s_tmem = tmem + kTmemS;
-      const uint32_t p_tmem = tmem + kTmemP;
       bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag);
+      // S(j) into S buffer j%2; it is issued after P.V(j-2), which read P(j-2)
+      // from the same columns (the tensor pipe runs a thread's MMAs in order).
+      auto issue_s = [&](int j) -> bool {
+        const int ks = j % kKStages;
+        if (!mbar_wait(bar(K_FULL + ks), (j / kKStages) & 1, abort_flag)) return false;
+        tc_fence_after();
+        const uint64_t kd = kd0 + static_cast<uint64_t>(ks * (kKVStageBytes >> 4));
+        const uint32_t dst = s_tmem + 64 * (j & 1);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t qo = ((kk >> 2) * (kQBytes / 2) + (kk & 3) * 32) >> 4;
+          const uint64_t ko = ((kk >> 2) * (kKVStageBytes / 2) + (kk & 3) * 32) >> 4;
+          mma_f16_ss(dst, qd + qo, kd + ko, kIdescQK, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(K_FREE + ks));
+        mma_commit(bar(S_FULL + (j & 1)));
+        return true;
+      };
       auto issue_pv = [&](int i) -> bool {
         const int pb = i & 1;
         if (!mbar_wait(bar(P_FULL + pb), (i >> 1) & 1, abort_flag)) return false;
         if (!mbar_wait(bar(V_FULL + pb), (i >> 1) & 1, abort_flag)) return false;
         tc_fence_after();
         const uint64_t vd = vd0 + static_cast<uint64_t>(pb * (kKVStageBytes >> 4));
-        const uint32_t pa = p_tmem + 32 * pb;
+        const uint32_t pa = s_tmem + 64 * pb;
         mma_f16_ts(tmem, pa, vd, kIdescPV, i > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 1; kk < 4; ++kk) mma_f16_ts(tmem, pa + 8 * kk, vd + kk * (2048 >> 4), kIdescPV, 1u);
-        mma_commit(bar(P_EMPTY + pb));
+        mma_commit(bar(PV_DONE + pb));
         return true;
       };
+      if (ok && n >= 1) ok = issue_s(0);
       for (int j = 0; ok && j < n; ++j) {
-        const int ks = j % kKStages;
-        if (!mbar_wait(bar(K_FULL + ks), (j / kKStages) & 1, abort_flag)) { ok = false; break; }
-        if (!mbar_wait(bar(S_EMPTY), (j & 1) ^ 1, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const uint64_t kd = kd0 + static_cast<uint64_t>(ks * (kKVStageBytes >> 4));
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t qo = ((kk >> 2) * (kQBytes / 2) + (kk & 3) * 32) >> 4;
-          const uint64_t ko = ((kk >> 2) * (kKVStageBytes / 2) + (kk & 3) * 32) >> 4;
-          mma_f16_ss(s_tmem, qd + qo, kd + ko, kIdescQK, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(bar(S_FULL + ks));
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        if (j + 1 < n && !issue_s(j + 1)) { ok = false; break; }
+        if (!issue_pv(j)) { ok = false; break; }
       }
-      if (ok && n >= 1) issue_pv(n - 1);
       // Whatever was issued must finish before TMEM is released.
       mma_commit(bar(MMA_DONE));
       mbar_wait_drain(bar(MMA_DONE), 0);
@@ -357,26 +367,22 @@ __global__ void __launch_bounds__(kThreads, 2)
       // and leaves the exponential unit to the other warps of its SM
       // sub-partition.
       const bool dead = __all_sync(0xffffffffu, nvalid == 0);
-      ok = mbar_wait_warp(bar(S_FULL + j % kKStages), (j / kKStages) & 1, abort_flag);
+      const int sb = j & 1;
+      const uint32_t ts = tl + kTmemS + 64 * sb;
+      ok = mbar_wait_warp(bar(S_FULL + sb), (j >> 1) & 1, abort_flag);
       if (!ok) break;
       tc_fence_after();
       uint32_t pk[32];
       bool rescale = false;
       float alpha = 1.0f;
       if (dead) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(S_EMPTY));
 #pragma unroll
         for (int c = 0; c < 32; ++c) pk[c] = 0u;
       } else {
         uint32_t sr0[32], sr1[32];
-        tmem_ld32(tl + kTmemS, sr0);
-        tmem_ld32(tl + kTmemS + 32, sr1);
+        tmem_ld32(ts, sr0);
+        tmem_ld32(ts + 32, sr1);
         tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(S_EMPTY));
         float x[64];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
@@ -402,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // O must not change under a running P.V: rescale only after P.V(j-1).
       if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
         const int pb1 = (j - 1) & 1;
-        ok = mbar_wait_warp(bar(P_EMPTY + pb1), ((j - 1) >> 1) & 1, abort_flag);
+        ok = mbar_wait_warp(bar(PV_DONE + pb1), ((j - 1) >> 1) & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll 1
@@ -416,20 +422,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tmem_wait_st();
       }
-      // P buffer j&1 was last read by P.V(j-2).
-      const int pb = j & 1;
-      ok = mbar_wait_warp(bar(P_EMPTY + pb), ((j >> 1) & 1) ^ 1, abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      tmem_st32(tl + kTmemP + 32 * pb, pk);
+      // P(j) over S(j) (already read into registers).
+      tmem_st32(ts, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(P_FULL + pb));
+      if (lane == 0) mbar_arrive(bar(P_FULL + sb));
     }
     // Epilogue: O / l, each thread stores its own row (256 bytes).
     if (ok && n >= 1) {
-      ok = mbar_wait(bar(P_EMPTY + ((n - 1) & 1)), ((n - 1) >> 1) & 1, abort_flag);
+      ok = mbar_wait(bar(PV_DONE + ((n - 1) & 1)), ((n - 1) >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
     } else if (ok) {
