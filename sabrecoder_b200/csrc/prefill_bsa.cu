@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int empty0 = is_k ? K_FREE : PV_DONE;
       const uint32_t ring = sbase + (is_k ? kKOff : kVOff);
       const CUtensorMap* map = is_k ? &tmK : &tmV;
-      int issued[kKStages] = {0, 0, 0};
+      int issued[kKStages] = {};
       UnionIter it(bits, bits + kWords, nw);
       for (int j = 0;; ++j) {
         const int kt = it.next();
