@@ -8,26 +8,27 @@
 //
 // Design (one CTA = 128 query rows of one head; 224 threads; 2 CTAs per SM):
 //   warps 0-3  softmax + epilogue; thread t owns query row t = TMEM lane t
-//   warp 4     TMA producer for Q and K (3-stage ring, a stage is released as
-//              soon as the S = Q K^T that read it completes)
+//   warp 4     TMA producer for Q and K (2-stage ring: K stage j%2 is
+//              released by the commit that marks S buffer j%2 full)
 //   warp 5     TMEM allocator and single-thread tcgen05.mma issuer
 //   warp 6     TMA producer for V (2-stage ring, released when P.V completes)
 // Two S buffers, with P written over its own S: S(j+1) is issued right after
 // P.V(j-1) (which read P(j-1) from the columns S(j+1) overwrites; the tensor
 // pipe runs a thread's MMAs in issue order), so it is computed while the
 // softmax works on S(j), and the softmax never waits for a P buffer.
-// Commits per key tile: K_FREE[stage] and S_FULL[buffer] after S = Q K^T
-// (the K producer's "stage free" and the softmax's "S ready"), PV_DONE[buffer]
-// after P.V (the V producer's "stage free", and the softmax's wait before it
-// rescales O). Each barrier's next completion needs its waiter's own next
-// step, so no waiter can miss a phase.
+// Each commit costs the tensor pipe about as much as a small MMA, so a key
+// tile takes two: S_FULL[buffer] after S = Q K^T (the softmax's "S ready" and
+// the K producer's "stage free"), PV_DONE[buffer] after P.V (the V
+// producer's "stage free", and the softmax's wait before it rescales O).
+// Each barrier's next completion needs its waiter's own next step, so no
+// waiter can miss a phase.
 // TMEM (256 columns): O [0,128), S0 [128,192), S1 [192,256); P(j) (bf16
 // pairs) over the first 32 columns of S(j%2).
 //   S = Q K^T      M=128 N=64  K=128, A and B from shared memory
 //   O += P V       M=128 N=128 K=64,  A (P) from TMEM, B (V) from shared
 //                  memory (MN-major)
-// Shared memory (bytes): Q 32768 | K 3x16384 | V 2x16384 | key-tile bitmaps
-// 256 | barriers (~112.5 KB).
+// Shared memory (bytes): Q 32768 | K 2x16384 | V 2x16384 | key-tile bitmaps
+// 256 | barriers (~96.5 KB).
 // A CTA's fixed costs are kept off its critical path: the Q tile is
 // requested right after the barriers are set up, while the block lists are
 // still being read, and each softmax thread writes its finished output row
@@ -53,7 +54,7 @@ namespace prefill {
 constexpr int kD = 128;
 constexpr int kTileM = 128;
 constexpr int kTileN = 64;
-constexpr int kKStages = 3;
+constexpr int kKStages = 2;
 constexpr int kVStages = 2;
 constexpr int kMaxKeyTiles = 1024;  // seq_len <= 65536
 constexpr int kWords = kMaxKeyTiles / 32;
@@ -66,13 +67,12 @@ constexpr int kKOff = kQOff + kQBytes;
 constexpr int kVOff = kKOff + kKStages * kKVStageBytes;
 constexpr int kBitsOff = kVOff + kVStages * kKVStageBytes;
 constexpr int kBarOff = kBitsOff + 2 * kWords * 4;
-static_assert(kVStages == 2, "V stage j%2 is released with S buffer j%2");
+static_assert(kKStages == 2 && kVStages == 2, "K and V stage j%2 go with S buffer j%2");
 enum Bar {
   Q_FULL = 0,
   K_FULL = 1,                     // [kKStages]
   V_FULL = K_FULL + kKStages,     // [2]
-  K_FREE = V_FULL + kVStages,     // [kKStages] S(j) done: K stage j%kKStages free
-  S_FULL = K_FREE + kKStages,     // [2] S(j) done in S buffer j%2
+  S_FULL = V_FULL + kVStages,     // [2] S(j) done in S buffer j%2; also "K stage j%2 free"
   P_FULL = S_FULL + 2,            // [2] P(j) stored over S buffer j%2 (one arrival per softmax warp)
   PV_DONE = P_FULL + 2,           // [2] P.V(j) done: V stage j%2 free
   MMA_DONE = PV_DONE + 2,
@@ -193,10 +193,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   for (int i = tid; i < 2 * kWords; i += kThreads) bits[i] = 0u;
   if (warp == 4 && lane == 0) {
     mbar_init(bar(Q_FULL), 1);
-    for (int s = 0; s < kKStages; ++s) {
-      mbar_init(bar(K_FULL + s), 1);
-      mbar_init(bar(K_FREE + s), 1);
-    }
+    for (int s = 0; s < kKStages; ++s) mbar_init(bar(K_FULL + s), 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(V_FULL + s), 1);
       mbar_init(bar(S_FULL + s), 1);
@@ -258,11 +255,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool is_k = (warp == 4);
       const int stages = is_k ? kKStages : kVStages;
       const int full0 = is_k ? K_FULL : V_FULL;
-      // K stage s is free when K_FREE[s] completes, V stage s when PV_DONE[s] does.
-      const int empty0 = is_k ? K_FREE : PV_DONE;
+      // K stage s is free when S_FULL[s] completes, V stage s when PV_DONE[s] does.
+      const int empty0 = is_k ? S_FULL : PV_DONE;
       const uint32_t ring = sbase + (is_k ? kKOff : kVOff);
       const CUtensorMap* map = is_k ? &tmK : &tmV;
-      int issued[kKStages] = {};
+      int issued[kKStages > kVStages ? kKStages : kVStages] = {};
       UnionIter it(bits, bits + kWords, nw);
       for (int j = 0;; ++j) {
         const int kt = it.next();
@@ -306,7 +303,6 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint64_t ko = ((kk >> 2) * (kKVStageBytes / 2) + (kk & 3) * 32) >> 4;
           mma_f16_ss(dst, qd + qo, kd + ko, kIdescQK, kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar(K_FREE + ks));
         mma_commit(bar(S_FULL + (j & 1)));
         return true;
       };
