@@ -9,7 +9,7 @@
 // Design (one CTA = 128 query rows of one head; 224 threads; 2 CTAs per SM):
 //   warps 0-3  softmax + epilogue; thread t owns query row t = TMEM lane t
 //   warp 4     TMA producer for Q and K (2-stage ring: K stage j%2 is
-//              released by the commit that marks S buffer j%2 full)
+//              released once S(j) has completed)
 //   warp 5     TMEM allocator and single-thread tcgen05.mma issuer
 //   warp 6     TMA producer for V (2-stage ring, released when P.V completes)
 // Two S buffers, with P written over its own S: S(j+1) is issued right after
@@ -17,11 +17,14 @@
 // pipe runs a thread's MMAs in issue order), so it is computed while the
 // softmax works on S(j), and the softmax never waits for a P buffer.
 // Each commit costs the tensor pipe about as much as a small MMA, so a key
-// tile takes two: S_FULL[buffer] after S = Q K^T (the softmax's "S ready" and
-// the K producer's "stage free"), PV_DONE[buffer] after P.V (the V
-// producer's "stage free", and the softmax's wait before it rescales O).
-// Each barrier's next completion needs its waiter's own next step, so no
-// waiter can miss a phase.
+// tile takes one: C(j), issued after P.V(j) and S(j+2), on DONE[j%2] (S(0)
+// and S(1) commit to PRO[0], PRO[1]). C(j) is the softmax's "S(j+2) ready",
+// the V producer's "stage j%2 free", the K producer's "stage j%2 free" for
+// K(j+4), and the softmax's wait before it rescales O or reads it out.
+// Every waiter takes each barrier's completions in order and a barrier's
+// next completion needs its waiter's own next step, so a parity wait never
+// confuses two phases (tests/test_prefill_protocol.py checks the protocol
+// under random schedules).
 // TMEM (256 columns): O [0,128), S0 [128,192), S1 [192,256); P(j) (bf16
 // pairs) over the first 32 columns of S(j%2).
 //   S = Q K^T      M=128 N=64  K=128, A and B from shared memory
@@ -72,10 +75,10 @@ enum Bar {
   Q_FULL = 0,
   K_FULL = 1,                     // [kKStages]
   V_FULL = K_FULL + kKStages,     // [2]
-  S_FULL = V_FULL + kVStages,     // [2] S(j) done in S buffer j%2; also "K stage j%2 free"
-  P_FULL = S_FULL + 2,            // [2] P(j) stored over S buffer j%2 (one arrival per softmax warp)
-  PV_DONE = P_FULL + 2,           // [2] P.V(j) done: V stage j%2 free
-  MMA_DONE = PV_DONE + 2,
+  PRO = V_FULL + kVStages,        // [2] S(0), S(1) done (one completion each)
+  DONE = PRO + 2,                 // [2] commit C(j) on DONE[j%2]: P.V(j) and S(j+2) done
+  P_FULL = DONE + 2,              // [2] P(j) stored over S buffer j%2 (one arrival per softmax warp)
+  MMA_DONE = P_FULL + 2,
   NUM_BARS = MMA_DONE + 1
 };
 constexpr int kMiscOff = kBarOff + NUM_BARS * 8;
@@ -196,9 +199,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int s = 0; s < kKStages; ++s) mbar_init(bar(K_FULL + s), 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(V_FULL + s), 1);
-      mbar_init(bar(S_FULL + s), 1);
+      mbar_init(bar(PRO + s), 1);
+      mbar_init(bar(DONE + s), 1);
       mbar_init(bar(P_FULL + s), 4);
-      mbar_init(bar(PV_DONE + s), 1);
     }
     mbar_init(bar(MMA_DONE), 1);
     fence_mbar_init();
@@ -255,8 +258,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool is_k = (warp == 4);
       const int stages = is_k ? kKStages : kVStages;
       const int full0 = is_k ? K_FULL : V_FULL;
-      // K stage s is free when S_FULL[s] completes, V stage s when PV_DONE[s] does.
-      const int empty0 = is_k ? S_FULL : PV_DONE;
+      // DONE[b]'s k-th completion is C(b + 2(k-1)): K(j) may overwrite stage
+      // j%2 after S(j-2) (PRO[j-2] for j < 4, else in C(j-4)), V(j) after
+      // P.V(j-2) (in C(j-2)). Every waiter takes a barrier's completions in
+      // order, so no parity wait can mistake one for another.
       const uint32_t ring = sbase + (is_k ? kKOff : kVOff);
       const CUtensorMap* map = is_k ? &tmK : &tmV;
       int issued[kKStages > kVStages ? kKStages : kVStages] = {};
@@ -265,7 +270,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int kt = it.next();
         if (kt < 0) break;
         const int s = j % stages;
-        if (!mbar_wait(bar(empty0 + s), ((j / stages) & 1) ^ 1, abort_flag)) break;
+        if (j >= 2) {
+          const int wb = is_k ? (j < 4 ? PRO + (j - 2) : DONE + s) : DONE + s;
+          const int par = is_k ? (j < 4 ? 0 : (j >> 1) & 1) : ((j >> 1) - 1) & 1;
+          if (!mbar_wait(bar(wb), par, abort_flag)) break;
+        }
         mbar_arrive_expect_tx(bar(full0 + s), kKVStageBytes);
         const uint32_t dst = ring + s * kKVStageBytes;
         tma_load_4d(dst, map, bar(full0 + s), 0, kt * 64, hk, b);
@@ -291,9 +300,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag);
       // S(j) into S buffer j%2; it is issued after P.V(j-2), which read P(j-2)
       // from the same columns (the tensor pipe runs a thread's MMAs in order).
+      // One commit per key tile: C(j) after P.V(j) and S(j+2), on DONE[j%2];
+      // S(0) and S(1) commit to PRO[0], PRO[1].
       auto issue_s = [&](int j) -> bool {
-        const int ks = j % kKStages;
-        if (!mbar_wait(bar(K_FULL + ks), (j / kKStages) & 1, abort_flag)) return false;
+        const int ks = j & 1;
+        if (!mbar_wait(bar(K_FULL + ks), (j >> 1) & 1, abort_flag)) return false;
         tc_fence_after();
         const uint64_t kd = kd0 + static_cast<uint64_t>(ks * (kKVStageBytes >> 4));
         const uint32_t dst = s_tmem + 64 * (j & 1);
@@ -303,7 +314,6 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint64_t ko = ((kk >> 2) * (kKVStageBytes / 2) + (kk & 3) * 32) >> 4;
           mma_f16_ss(dst, qd + qo, kd + ko, kIdescQK, kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar(S_FULL + (j & 1)));
         return true;
       };
       auto issue_pv = [&](int i) -> bool {
@@ -316,13 +326,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         mma_f16_ts(tmem, pa, vd, kIdescPV, i > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 1; kk < 4; ++kk) mma_f16_ts(tmem, pa + 8 * kk, vd + kk * (2048 >> 4), kIdescPV, 1u);
-        mma_commit(bar(PV_DONE + pb));
         return true;
       };
-      if (ok && n >= 1) ok = issue_s(0);
+      for (int j = 0; ok && j < 2 && j < n; ++j) {
+        ok = issue_s(j);
+        if (ok) mma_commit(bar(PRO + j));
+      }
       for (int j = 0; ok && j < n; ++j) {
-        if (j + 1 < n && !issue_s(j + 1)) { ok = false; break; }
         if (!issue_pv(j)) { ok = false; break; }
+        if (j + 2 < n && !issue_s(j + 2)) { ok = false; break; }
+        mma_commit(bar(DONE + (j & 1)));
       }
       // Whatever was issued must finish before TMEM is released.
       mma_commit(bar(MMA_DONE));
@@ -365,7 +378,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool dead = __all_sync(0xffffffffu, nvalid == 0);
       const int sb = j & 1;
       const uint32_t ts = tl + kTmemS + 64 * sb;
-      ok = mbar_wait_warp(bar(S_FULL + sb), (j >> 1) & 1, abort_flag);
+      // S(j): PRO[j] for j < 2, else in C(j-2)
+      ok = j < 2 ? mbar_wait_warp(bar(PRO + j), 0, abort_flag)
+                 : mbar_wait_warp(bar(DONE + sb), ((j >> 1) - 1) & 1, abort_flag);
       if (!ok) break;
       tc_fence_after();
       uint32_t pk[32];
@@ -403,8 +418,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 
       // O must not change under a running P.V: rescale only after P.V(j-1).
       if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
-        const int pb1 = (j - 1) & 1;
-        ok = mbar_wait_warp(bar(PV_DONE + pb1), ((j - 1) >> 1) & 1, abort_flag);
+        // P.V(j-1) is in C(j-1)
+        ok = mbar_wait_warp(bar(DONE + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll 1
@@ -427,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // Epilogue: O / l, each thread stores its own row (256 bytes).
     if (ok && n >= 1) {
-      ok = mbar_wait(bar(PV_DONE + ((n - 1) & 1)), ((n - 1) >> 1) & 1, abort_flag);
+      ok = mbar_wait(bar(DONE + ((n - 1) & 1)), ((n - 1) >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
     } else if (ok) {
