@@ -1122,8 +1122,9 @@ def run_decode_op(args, rank, world, dist):
     nbytes = rows * H * 128 * 2 * 2 + 2 * Hq * 128 * 2
     gbs = nbytes / ms / 1e6
     _, _, hbm, which = measured_peaks()
-    traffic = profile_traffic(f"decode_bsa_{args.workload}_{args.decode_op}")
-    kern = ("sabre decode_gqa_kernel + decode_combine_kernel" if Hq // H >= 3
+    gqa = Hq // H >= 3  # the tensor-core kernel serves groups of three or more query heads per KV head
+    traffic = profile_traffic(f"{'decode_gqa' if gqa else 'decode_bsa'}_{args.workload}_{args.decode_op}")
+    kern = ("sabre decode_gqa_kernel + decode_combine_kernel" if gqa
             else "sabre decode_bulk_kernel + decode_combine_kernel")
     if rank == 0:
         print(json.dumps({"metric": "decode attention GB/s (single op)", "value": gbs, "unit": "GB/s",
