@@ -199,17 +199,6 @@ def _until(toks: Sequence[_Tok], i: int, end: int, stops: Tuple[str, ...]) -> in
     return end
 
 
-@dataclass
-class _Decl:
-    kind: str           # "import", "class", "type" (walked, no chunk), "func", "field"
-    first: int          # first token
-    last: int           # last token
-    name: str = ""
-    name_tok: int = -1  # token of the declared name
-    body: Tuple[int, int] = (-1, -1)  # tokens strictly inside the body braces
-    header_end: int = -1
-
-
 class _Scanner:
     """Declarations of a Java or C# token stream (see the module docstring)."""
 
