@@ -72,6 +72,9 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const Params p) 
   // Let the combine kernel (a programmatic dependent launch) become resident
   // now: its griddepcontrol.wait still waits for this whole grid.
   if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // Launched as a programmatic dependent of the previous kernel: nothing
+  // below may read before that kernel's writes are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int split = blockIdx.x;
   const int hk = blockIdx.y;
   const int b = blockIdx.z;
@@ -301,13 +304,6 @@ __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Para
   auto full_bar = [&](int s) -> uint32_t { return sbase + kBulkBarOff + 8u * s; };
   auto empty_bar = [&](int s) -> uint32_t { return sbase + kBulkBarOff + 8u * (kBulkStages + s); };
 
-  // The sequence length, the list count and the split's first index are
-  // independent loads, issued together before the barrier set-up.
-  const int T_valid = min(p.seq_lens[b], p.Tmax);
-  int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];
-  const int j0 = split * p.bps;
-  const int32_t* ip = p.idx + b * p.idx_sb + hk * p.idx_sh;
-  const int first_kb = (warp == kBulkConsumerWarps && lane == 0 && j0 < p.max_active) ? ip[j0 * p.idx_sk] : -1;
   if (tid == 0) {
     *abort_flag = 0;
     for (int s = 0; s < kBulkStages; ++s) {
@@ -317,6 +313,16 @@ __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Para
     fence_mbar_init();
   }
   __syncthreads();
+  // Launched as a programmatic dependent of the previous kernel: the set-up
+  // above overlaps its tail; nothing below may read before its writes are
+  // visible. The sequence length, the list count and the split's first
+  // index are then independent loads, issued together.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int T_valid = min(p.seq_lens[b], p.Tmax);
+  int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];
+  const int j0 = split * p.bps;
+  const int32_t* ip = p.idx + b * p.idx_sb + hk * p.idx_sh;
+  const int first_kb = (warp == kBulkConsumerWarps && lane == 0 && j0 < p.max_active) ? ip[j0 * p.idx_sk] : -1;
   cnt = min(cnt, p.max_active);
   const int j1 = min(j0 + p.bps, cnt);
   const T* kbase = static_cast<const T*>(p.kc) + b * p.k_sb + hk * p.k_sh;
@@ -491,6 +497,9 @@ __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Para
 // not wait on one another; the sums run in split order as before.
 template <typename T>
 __global__ void __launch_bounds__(kD) decode_combine_kernel(const Params p) {
+  // The next decode call's split kernel (a programmatic dependent too) may
+  // start its set-up now; it waits for this grid before touching memory.
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float sm_m[kMaxSplits], sm_l[kMaxSplits];
   const int bh = blockIdx.x;
@@ -528,11 +537,20 @@ __global__ void __launch_bounds__(kD) decode_combine_kernel(const Params p) {
 
 template <typename T, int G>
 static void launch_split(const Params& p, bool bulk, cudaStream_t s) {
-  dim3 grid(p.splits, p.Hkv, p.B);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits, p.Hkv, p.B);
+  cfg.blockDim = dim3(bulk ? kBulkThreads : kThreads);
+  cfg.dynamicSmemBytes = bulk ? kBulkSmem : 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (bulk)
-    decode_bulk_kernel<T, G><<<grid, kBulkThreads, kBulkSmem, s>>>(p);
+    cudaLaunchKernelEx(&cfg, decode_bulk_kernel<T, G>, p);
   else
-    decode_split_kernel<T, G><<<grid, kThreads, 0, s>>>(p);
+    cudaLaunchKernelEx(&cfg, decode_split_kernel<T, G>, p);
 }
 
 // Groups of at least this many query heads per KV head decode on the tensor

@@ -74,30 +74,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int b = blockIdx.z;
   const int g = p.Hq / p.Hkv;
 
-  // The start-up global loads are independent and issued together: the
-  // sequence length, the list count, the split's first index (prefetched for
-  // the producers' list walks) and this thread's 16 bytes of Q.
-  const int T_valid = min(p.seq_lens[b], p.Tmax);
-  int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];
-  const int j0 = split * p.bps;
-  const int32_t* ip = p.idx + b * p.idx_sb + hk * p.idx_sh;
-  if (tid == 32 && j0 < p.max_active) asm volatile("prefetch.global.L1 [%0];" ::"l"(ip + j0 * p.idx_sk));
-  // Q: row r < g is query head hk*g + r, stored as the 128-byte-swizzled
-  // K-major layout a TMA load would produce (16-byte chunk c of row r of a
-  // d-half at r*128 + ((c ^ (r & 7)) << 4)); rows g..7 are zero.
-  static_assert(2 * 8 * 8 == kThreads, "one 16-byte chunk of Q per thread");
-  {
-    const int c = tid & 7;
-    const int r = (tid >> 3) & 7;
-    const int dh = tid >> 6;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (r < g) {
-      const T* qp = static_cast<const T*>(p.q) + b * p.q_sb + (hk * g + r) * p.q_sh + dh * 64 + c * 8;
-      v = *reinterpret_cast<const uint4*>(qp);
-    }
-    *reinterpret_cast<uint4*>(smem + kQOff + dh * (kQBytes / 2) + r * 128 + ((c ^ (r & 7)) << 4)) = v;
-  }
-  fence_proxy_async_smem();  // the tensor cores read Q through the async proxy
   if (tid == 0) {
     const bool bad = (sbase & 1023u) != 0u;
     *abort_flag = bad ? 1 : 0;
@@ -128,6 +104,35 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const bool start_ok = (*abort_flag == 0);
+  // Launched as a programmatic dependent of the previous kernel: the set-up
+  // above overlaps its tail; nothing below may read before its writes are
+  // visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The start-up global loads are independent and issued together: the
+  // sequence length, the list count, the split's first index (prefetched for
+  // the producers' list walks) and this thread's 16 bytes of Q.
+  const int T_valid = min(p.seq_lens[b], p.Tmax);
+  int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];
+  const int j0 = split * p.bps;
+  const int32_t* ip = p.idx + b * p.idx_sb + hk * p.idx_sh;
+  if (tid == 32 && j0 < p.max_active) asm volatile("prefetch.global.L1 [%0];" ::"l"(ip + j0 * p.idx_sk));
+  // Q: row r < g is query head hk*g + r, stored as the 128-byte-swizzled
+  // K-major layout a TMA load would produce (16-byte chunk c of row r of a
+  // d-half at r*128 + ((c ^ (r & 7)) << 4)); rows g..7 are zero.
+  static_assert(2 * 8 * 8 == kThreads, "one 16-byte chunk of Q per thread");
+  {
+    const int c = tid & 7;
+    const int r = (tid >> 3) & 7;
+    const int dh = tid >> 6;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (r < g) {
+      const T* qp = static_cast<const T*>(p.q) + b * p.q_sb + (hk * g + r) * p.q_sh + dh * 64 + c * 8;
+      v = *reinterpret_cast<const uint4*>(qp);
+    }
+    *reinterpret_cast<uint4*>(smem + kQOff + dh * (kQBytes / 2) + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+  }
+  fence_proxy_async_smem();  // the tensor cores read Q through the async proxy
+  __syncthreads();
 
   cnt = min(cnt, p.max_active);
   const int j1 = min(j0 + p.bps, cnt);
@@ -340,6 +345,21 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 // Launches decode_gqa_kernel and the combine kernel; p carries the split
 // count and partial buffers chosen by the entry point.
+template <typename K, typename... A>
+static cudaError_t launch_pdl(dim3 grid, int threads, int smem, cudaStream_t s, K kernel, A... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 static int decode_gqa_launch(const Params& p, int dtype, cudaStream_t s) {
   CUtensorMap mk, mv;
   int st;
@@ -362,12 +382,12 @@ static int decode_gqa_launch(const Params& p, int dtype, cudaStream_t s) {
   cfg.numAttrs = 1;
   if (dtype == SABRE_BF16) {
     if ((st = ensure_smem_attr(gqa::decode_gqa_kernel<__nv_bfloat16>, gqa::kSmemBytes)) != SABRE_OK) return st;
-    gqa::decode_gqa_kernel<__nv_bfloat16><<<grid, gqa::kThreads, gqa::kSmemBytes, s>>>(mk, mv, p);
+    SABRE_CUDA_TRY(launch_pdl(grid, gqa::kThreads, gqa::kSmemBytes, s, gqa::decode_gqa_kernel<__nv_bfloat16>, mk, mv, p));
     SABRE_CUDA_TRY(cudaGetLastError());
     SABRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_combine_kernel<__nv_bfloat16>, p));
   } else {
     if ((st = ensure_smem_attr(gqa::decode_gqa_kernel<__half>, gqa::kSmemBytes)) != SABRE_OK) return st;
-    gqa::decode_gqa_kernel<__half><<<grid, gqa::kThreads, gqa::kSmemBytes, s>>>(mk, mv, p);
+    SABRE_CUDA_TRY(launch_pdl(grid, gqa::kThreads, gqa::kSmemBytes, s, gqa::decode_gqa_kernel<__half>, mk, mv, p));
     SABRE_CUDA_TRY(cudaGetLastError());
     SABRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_combine_kernel<__half>, p));
   }
