@@ -372,10 +372,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       const int nvalid = vis ? min(64, max(0, r_abs - kt * 64 + 1)) : 0;
       // A warp whose 32 rows see no key of this tile (the tile is listed
-      // only by the other half, or lies wholly after the rows) stores P = 0
-      // and leaves the exponential unit to the other warps of its SM
-      // sub-partition.
-      const bool dead = __all_sync(0xffffffffu, nvalid == 0);
+      // only by the other half, lies wholly after the rows, or their token
+      // masks hide it) stores P = 0 and leaves the exponential unit to the
+      // other warps of its SM sub-partition.
+      const bool dead = __all_sync(0xffffffffu, nvalid == 0 || (kTok && tw == 0ull));
       const int sb = j & 1;
       const uint32_t ts = tl + kTmemS + 64 * sb;
       // S(j): PRO[j] for j < 2, else in C(j-2)
