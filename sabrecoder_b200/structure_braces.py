@@ -343,7 +343,7 @@ class _Scanner:
         while name_tok < end and t[name_tok].kind != "id":
             name_tok += 1
         name = t[name_tok].text if name_tok < end else "unknown"
-        j = name_tok + 1
+        j = min(name_tok + 1, end)
         while j < end and t[j].text not in ("{", ";"):
             j = _match(t, j) + 1 if t[j].text in ("(", "[") else j + 1
         if self.java:
@@ -655,6 +655,7 @@ class BraceReferenceAnalyzer:
                 self._add(t[start].line, last_ident(start, callee_end), "call")
         # inheritance
         for first, hend, kind in sc.classes:
+            hend = min(hend, n)  # a header cut off by the end of the file
             names: List[str] = []
             if kind == 0:  # Java class: extends (last identifier) + implements (every type identifier)
                 j = first

@@ -11,6 +11,8 @@ documented node shapes (parity unpinned).
 
 import random
 
+import pytest
+
 import numpy as np
 
 from sabrecoder_b200.structure_braces import StructureAnalyzer, StructureSegmenter
@@ -308,3 +310,144 @@ def test_language_detection_follows_the_reference_heuristic():
     assert detect_language(java_only) == "java"
     assert _view(StructureSegmenter().segment_code(java_only)) == _view(StructureSegmenter().segment_code(java_only, "java"))
     assert _view(StructureSegmenter().segment_code(CSHARP)) == _view(StructureSegmenter().segment_code(CSHARP, "C#"))
+
+
+JAVA_MORE = """package demo.more;
+
+import java.util.*;
+import java.util.function.Function;
+
+@SuppressWarnings({"unchecked", "rawtypes"})
+public final class Registry<K extends Comparable<K>, V> implements Iterable<Map.Entry<K, List<V>>> {
+    private static final Map<String, Integer> CODES = new HashMap<>();
+    static {
+        CODES.put("a", 1);
+    }
+    private final Map<K, List<V>> map = new TreeMap<>((a, b) -> a.compareTo(b));
+
+    public <R> List<R> mapAll(Function<? super V, ? extends R> fn) {
+        List<R> out = new ArrayList<>();
+        map.values().forEach(vs -> vs.forEach(v -> out.add(fn.apply(v))));
+        return out;
+    }
+
+    @Override
+    public Iterator<Map.Entry<K, List<V>>> iterator() { return map.entrySet().iterator(); }
+
+    int kind(Object o) {
+        return switch (o) {
+            case Integer i when i > 0 -> 1;
+            case String s -> { yield s.length(); }
+            default -> 0;
+        };
+    }
+
+    record Pair<A, B>(A first, B second) {
+        Pair { Objects.requireNonNull(first); }
+        static <T> Pair<T, T> twin(T t) { return new Pair<>(t, t); }
+    }
+
+    interface Visitor<T> {
+        T visit(Object node);
+        default T fallback() { return null; }
+    }
+
+    abstract static class Node {
+        abstract int size();
+        protected void touch() { mapAll(null); }
+    }
+}
+"""
+
+CSHARP_MORE = """using System;
+using System.Collections.Generic;
+using static System.Math;
+
+namespace Demo.More;
+
+[Obsolete("use V2", false)]
+public sealed class Cache<TKey, TValue> : IDisposable where TKey : notnull
+{
+    private readonly Dictionary<TKey, TValue> _items = new();
+    public event EventHandler? Changed;
+
+    public int Count
+    {
+        get { return _items.Count; }
+    }
+
+    public TValue this[TKey key] => _items[key];
+
+    public bool TryGet(TKey key, out TValue value) => _items.TryGetValue(key, out value);
+
+    [Conditional("DEBUG")]
+    public void Dump()
+    {
+        foreach (var (k, v) in _items) { Console.WriteLine($"{k}={v}"); }
+        Changed?.Invoke(this, EventArgs.Empty);
+    }
+
+    public async System.Threading.Tasks.Task<int> LoadAsync() { await System.Threading.Tasks.Task.Yield(); return Max(1, 2); }
+
+    public void Dispose() => _items.Clear();
+}
+
+public record Point(int X, int Y)
+{
+    public double Norm() => Sqrt(X * X + Y * Y);
+}
+"""
+
+
+def _well_formed(code, chunks):
+    n = len(code.split("\n"))
+    for c in chunks:
+        assert 1 <= c.start_line <= c.end_line <= n, (c.name, c.start_line, c.end_line, n)
+    classes = {c.name: c for c in chunks if c.chunk_type.name == "CLASS"}
+    for c in chunks:
+        if c.chunk_type.name == "METHOD" and c.parent_name in classes:
+            p = classes[c.parent_name]
+            assert p.start_line <= c.start_line and c.end_line <= p.end_line, (c.name, c.parent_name)
+
+
+def test_broader_java_syntax():
+    ch = StructureSegmenter().segment_code(JAVA_MORE, "java")
+    _well_formed(JAVA_MORE, ch)
+    sem = [(c.chunk_type.name, c.name, c.parent_name) for c in ch if c.chunk_type.name != "MODULE_CODE"]
+    names = [n for _, n, _ in sem]
+    # generic methods, overrides and switch expressions are methods; the record's compact constructor and
+    # static factory are walked with the outer class as parent (records are no chunks)
+    for want in (("CLASS", "Registry", None), ("METHOD", "mapAll", "Registry"), ("METHOD", "iterator", "Registry"),
+                 ("METHOD", "kind", "Registry"), ("METHOD", "twin", "Registry"), ("CLASS", "Visitor", None),
+                 ("METHOD", "visit", "Visitor"), ("METHOD", "fallback", "Visitor"), ("CLASS", "Node", None),
+                 ("METHOD", "size", "Node"), ("METHOD", "touch", "Node")):
+        assert want in sem, (want, sem)
+    assert "Pair" not in [n for k, n, _ in sem if k == "CLASS"]
+    assert names.count("import") == 3
+    refs = StructureAnalyzer(ch, JAVA_MORE, "java").analyze()
+    by = {(ch[r.source_chunk_idx].name, ch[r.target_chunk_idx].name, r.ref_type) for r in refs}
+    assert ("touch", "mapAll", "call") in by
+
+
+def test_broader_csharp_syntax():
+    ch = StructureSegmenter().segment_code(CSHARP_MORE, "c_sharp")
+    _well_formed(CSHARP_MORE, ch)
+    sem = [(c.chunk_type.name, c.name, c.parent_name) for c in ch if c.chunk_type.name != "MODULE_CODE"]
+    for want in (("CLASS", "Cache", None), ("METHOD", "TryGet", "Cache"), ("METHOD", "Dump", "Cache"),
+                 ("METHOD", "Dispose", "Cache")):
+        assert want in sem, (want, sem)
+    # properties, indexers and events are no methods; records are walked without being chunks
+    assert not any(n in ("Count", "Changed", "this") for _, n, _ in sem)
+    assert ("METHOD", "Norm", None) in sem or any(n == "Norm" for _, n, _ in sem)
+    assert [n for _, n, _ in sem].count("import") == 3
+
+
+@pytest.mark.parametrize("lang,code", [("java", JAVA), ("java", JAVA_MORE), ("c_sharp", CSHARP), ("c_sharp", CSHARP_MORE)])
+def test_truncated_and_unbalanced_sources_do_not_fail(lang, code):
+    rnd = random.Random(0)
+    cuts = sorted({rnd.randrange(len(code)) for _ in range(25)}) + [len(code) // 2]
+    for cut in cuts:
+        for src in (code[:cut], code[:cut] + "}}}", "{{" + code[cut:], code.replace("}", "", 3)):
+            ch = StructureSegmenter().segment_code(src, lang)
+            _well_formed(src, ch)
+            StructureAnalyzer(ch, src, lang).analyze()
