@@ -147,6 +147,36 @@ def test_prefill_many_items_ragged(K, block):
     assert K.device_status() == 0
 
 
+def test_prefill_small_union_counts(K):
+    """128-row tiles whose union of key tiles is exactly 0, 1, 2, 3, 4 and 5
+    (the counts where the kernel's first S commits and its per-tile commits
+    meet), each tile on its own head; every wait completes (no timeout
+    recorded) and the rows match the oracle."""
+    gen = torch.Generator().manual_seed(41)
+    B, H, L, D, block = 1, 6, 768, 128, 64
+    q, k, v = (torch.randn(B, H, L, D, generator=gen).to(torch.bfloat16) for _ in range(3))
+    nb = L // block                       # 12 query blocks, 6 tiles of 128 rows
+    m = torch.zeros(B, H, nb, nb, dtype=torch.bool)
+    for h, n_union in enumerate(range(6)):
+        # tile 5 (query blocks 10 and 11): a union of exactly n_union key tiles
+        keys = list(range(n_union))
+        for qb in (10, 11):
+            for kb in keys:
+                m[0, h, qb, kb] = True
+        # the other tiles of the head keep their diagonal block only
+        for qb in range(10):
+            m[0, h, qb, qb] = True
+    idx, cnt = MO.block_indices_from_mask(m.numpy())
+    bi, bc = torch.from_numpy(idx), torch.from_numpy(cnt)
+    K.device_status(clear=True)
+    out = K.prefill_bsa(q.cuda(), k.cuda(), v.cuda(), bi.cuda(), bc.cuda(), block)
+    torch.cuda.synchronize()
+    assert K.device_status() == 0
+    ref = AO.sparse_prefill_fp32(q, k, v, bi, bc, block)
+    _close(out, ref)
+    assert out[0, 0, 640:768].abs().max().item() == 0.0   # union 0: nothing visible
+
+
 def test_prefill_config0_shape(K):
     """B=1, H=16, L=4096, D=128, block 64 with a structure mask + top-8."""
     gen = torch.Generator().manual_seed(0)
