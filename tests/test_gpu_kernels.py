@@ -295,7 +295,10 @@ def test_pooled_topk_bit_exact(K, B, Hq, Hkv, L, block, topk):
                                                          (1, 16, 16, 3000, 64, False), (2, 32, 8, 2000, 64, True),
                                                          (3, 24, 3, 1800, 128, False), (1, 32, 32, 4100, 64, True),
                                                          # a cache shorter than one 64-row tile
-                                                         (2, 8, 2, 40, 64, False)])
+                                                         (2, 8, 2, 40, 64, False),
+                                                         # blocks of three and four 64-row pieces: a split's
+                                                         # share may start and end inside a block
+                                                         (2, 14, 2, 2500, 192, False), (1, 8, 1, 4000, 256, True)])
 def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
     gen = torch.Generator().manual_seed(Tmax + Hq)
     D = 128
@@ -340,7 +343,8 @@ def test_decode_f16_vs_oracle(K, Hq, Hkv):
     _close(out, ref)
 
 
-@pytest.mark.parametrize("block,row_pad,Hq", [(32, 0, 4), (64, 128, 4), (64, 128, 14), (128, 64, 16)])
+@pytest.mark.parametrize("block,row_pad,Hq", [(32, 0, 4), (64, 128, 4), (64, 128, 14), (128, 64, 16),
+                                               (192, 128, 4)])
 def test_decode_strided_cache_vs_oracle(K, block, row_pad, Hq):
     """Caches whose rows are not contiguous per head (row stride > head_dim) or
     blocks that are not whole 64-row chunks take the register-streaming kernel;
