@@ -185,6 +185,21 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
+// L2 prefetch hints: the bytes go to L2 only, nothing reaches the SM, and no
+// result depends on them. Untiled: address 16-byte aligned, size a multiple
+// of 16. Tiled: the tensor map's box at the given coordinates.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* m, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tensor core / TMA) before signalling their consumer.
 __device__ __forceinline__ void fence_proxy_async_smem() {

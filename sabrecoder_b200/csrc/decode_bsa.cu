@@ -246,6 +246,32 @@ constexpr int kBulkBarOff = kBulkRingBytes;
 constexpr int kBulkSmem = kBulkBarOff + 2 * kBulkStages * 8 + 16;
 constexpr int kBulkTargetCtas = 2 * 148;
 
+// Chunks of its share a split CTA asks L2 for before griddepcontrol.wait
+// (two measured best of one to four).
+constexpr int kPrefetchChunks = 2;
+
+// Calls f(t, rows) for the first kPrefetchChunks 64-row chunks of a split's
+// share (entries j0 .. j1-1 of the list at ip), for L2 prefetches issued
+// before griddepcontrol.wait. The entries may still be written by the
+// previous kernel, so a value read here is only a hint: chunks are clamped
+// to the cache's Tmax rows and nothing else depends on them.
+template <typename F>
+__device__ __forceinline__ void prefetch_walk(const int32_t* ip, long long sk, int j0, int j1, int block, int Tmax,
+                                              F&& f) {
+  int kb[kPrefetchChunks];
+#pragma unroll
+  for (int i = 0; i < kPrefetchChunks; ++i) kb[i] = (j0 + i < j1) ? ip[(j0 + i) * sk] : -1;
+  int left = kPrefetchChunks;
+#pragma unroll
+  for (int i = 0; i < kPrefetchChunks; ++i) {
+    for (int sub = 0; sub < block / 64 && left > 0; ++sub, --left) {
+      const long long t = static_cast<long long>(kb[i]) * block + sub * 64;
+      if (kb[i] < 0 || t >= Tmax) break;
+      f(static_cast<int>(t), static_cast<int>(min(64LL, Tmax - t)));
+    }
+  }
+}
+
 // Walks the 64-row chunks of a split's share of one list: the same sequence
 // for the producer and the consumers.
 struct ChunkWalk {
@@ -313,10 +339,21 @@ __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Para
     fence_mbar_init();
   }
   __syncthreads();
+  if (warp == kBulkConsumerWarps && lane == 0 && kPrefetchChunks > 0) {
+    const T* kb0 = static_cast<const T*>(p.kc) + b * p.k_sb + hk * p.k_sh;
+    const T* vb0 = static_cast<const T*>(p.vc) + b * p.v_sb + hk * p.v_sh;
+    const int j0p = split * p.bps;
+    prefetch_walk(p.idx + b * p.idx_sb + hk * p.idx_sh, p.idx_sk, j0p, min(j0p + p.bps, p.max_active), p.block,
+                  p.Tmax, [&](int t, int rows) {
+                    bulk_prefetch_l2(kb0 + static_cast<long long>(t) * kD, static_cast<uint32_t>(rows) * kD * 2);
+                    bulk_prefetch_l2(vb0 + static_cast<long long>(t) * kD, static_cast<uint32_t>(rows) * kD * 2);
+                  });
+  }
   // Launched as a programmatic dependent of the previous kernel: the set-up
   // above overlaps its tail; nothing below may read before its writes are
-  // visible. The sequence length, the list count and the split's first
-  // index are then independent loads, issued together.
+  // visible (the prefetches above are hints). The sequence length, the list
+  // count and the split's first index are then independent loads, issued
+  // together.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int T_valid = min(p.seq_lens[b], p.Tmax);
   int cnt = p.cnt[b * p.cnt_sb + hk * p.cnt_sh];

@@ -104,9 +104,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const bool start_ok = (*abort_flag == 0);
+  if (tid == 32 && start_ok && kPrefetchChunks > 0) {
+    const int j0p = split * p.bps;
+    prefetch_walk(p.idx + b * p.idx_sb + hk * p.idx_sh, p.idx_sk, j0p, min(j0p + p.bps, p.max_active), p.block,
+                  p.Tmax, [&](int t, int) {
+                    tma_prefetch_l2_4d(&tmK, 0, t, hk, b);
+                    tma_prefetch_l2_4d(&tmK, 64, t, hk, b);
+                    tma_prefetch_l2_4d(&tmV, 0, t, hk, b);
+                    tma_prefetch_l2_4d(&tmV, 64, t, hk, b);
+                  });
+  }
   // Launched as a programmatic dependent of the previous kernel: the set-up
   // above overlaps its tail; nothing below may read before its writes are
-  // visible.
+  // visible (the L2 prefetches above are hints).
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // The start-up global loads are independent and issued together: the
   // sequence length, the list count, the split's first index (prefetched for
