@@ -1,8 +1,10 @@
 """CPU model check of the prefill kernel's mbarrier protocol (prefill_bsa.cu).
 
-Four roles run as programs of steps: the K producer, the V producer, the
-single-thread MMA issuer and the softmax warps (their four arrivals on a
-P_FULL barrier modelled as one). A wait on (barrier, parity) passes when the
+The roles run as programs of steps: the K producer, the V producer, the
+single-thread MMA issuer and each of the four softmax warps on its own (a
+warp whose rows do not list a tile runs ahead of the others, so warps can
+be at different key tiles; a P_FULL phase completes on its fourth arrival,
+and an arrival for a later phase landing in an open phase is an error). A wait on (barrier, parity) passes when the
 barrier's completion count has the other parity, as `mbarrier.try_wait.parity`
 does. TMA copies complete in any order; MMAs and commits complete in issue
 order. Random schedules must never deadlock and never break an ordering rule
@@ -14,6 +16,9 @@ wait whose parity names the wrong completion -- must be caught.
 import random
 
 import pytest
+
+
+WARPS = 4  # softmax warps; each arrives once per key tile on P_FULL[j%2]
 
 
 def _programs(n, rnd, flawed=False, rescale_prob=0.3):
@@ -43,7 +48,8 @@ def _programs(n, rnd, flawed=False, rescale_prob=0.3):
         def pv(i):
             yield ("wait", ("PF", i & 1), (i >> 1) & 1)
             yield ("wait", ("VF", i & 1), (i >> 1) & 1)
-            yield ("check", lambda s: ("V", i) in s and ("P", i) in s, f"PV{i} before P{i} / V{i}")
+            yield ("check", lambda s: ("V", i) in s and all(("P", i, w) in s for w in range(WARPS)),
+                   f"PV{i} before P{i} / V{i}")
             yield ("mma", ("PV", i))
 
         for j in range(min(2, n)):
@@ -55,7 +61,7 @@ def _programs(n, rnd, flawed=False, rescale_prob=0.3):
                 yield from s_(j + 2)
             yield ("commit", ("DONE", j & 1))
 
-    def softmax():
+    def softmax(w):
         for j in range(n):
             if j < 2:
                 yield ("wait", ("PRO", j), 0)
@@ -65,18 +71,21 @@ def _programs(n, rnd, flawed=False, rescale_prob=0.3):
             if j >= 1 and rnd.random() < rescale_prob:
                 yield ("wait", ("DONE", (j - 1) & 1), ((j - 1) >> 1) & 1)  # P.V(j-1) is in C(j-1)
                 yield ("check", lambda s, j=j: ("PV", j - 1) in s, f"O rescaled under PV{j - 1}")
-            yield ("done", ("P", j))
-            yield ("arrive", ("PF", j & 1))
+            yield ("done", ("P", j, w))
+            yield ("arrive", ("PF", j & 1), j)
         if n >= 1:
             yield ("wait", ("DONE", (n - 1) & 1), ((n - 1) >> 1) & 1)
             yield ("check", lambda s: ("PV", n - 1) in s, "O read out under the last P.V")
 
-    return {"kp": kp(), "vp": vp(), "mma": mma(), "softmax": softmax()}
+    progs = {"kp": kp(), "vp": vp(), "mma": mma()}
+    for w in range(WARPS):
+        progs[f"softmax{w}"] = softmax(w)
+    return progs
 
 
 def _run(n, seed, flawed=False):
     rnd = random.Random(seed)
-    count, done, tma, pipe = {}, set(), [], []
+    count, done, tma, pipe, pend = {}, set(), [], [], {}
     progs = _programs(n, rnd, flawed)
     cur = {k: next(g, None) for k, g in progs.items()}
     while True:
@@ -111,7 +120,13 @@ def _run(n, seed, flawed=False):
         elif op[0] == "done":
             done.add(op[1])
         elif op[0] == "arrive":
-            count[op[1]] = count.get(op[1], 0) + 1
+            got = pend.setdefault(op[1], [])
+            if got and got[0] != op[2]:
+                return f"violation: arrival for P{op[2]} in the phase of P{got[0]}"
+            got.append(op[2])
+            if len(got) == WARPS:
+                pend[op[1]] = []
+                count[op[1]] = count.get(op[1], 0) + 1
         cur[k] = next(progs[k], None)
 
 
