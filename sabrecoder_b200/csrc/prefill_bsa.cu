@@ -37,6 +37,9 @@
 // still being read, and each softmax thread writes its finished output row
 // straight to global memory with 16-byte stores (no staging, no wait for a
 // bulk store to drain before the CTA can exit).
+// Q is read once and O written once, so both go through L2 with an
+// evict-first policy: the K/V rows that other CTAs of the head still read
+// keep their place in L2.
 //
 // The key-tile list of a CTA is the union of the lists of the (one or two)
 // query blocks its rows belong to, kept as two 1024-bit bitmaps (one per
@@ -209,8 +212,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     tma_prefetch_desc(&tmV);
     if ((sbase & 1023u) == 0u) {
       mbar_arrive_expect_tx(bar(Q_FULL), kQBytes);
-      tma_load_4d(sbase + kQOff, &tmQ, bar(Q_FULL), 0, r0, h, b);
-      tma_load_4d(sbase + kQOff + kQBytes / 2, &tmQ, bar(Q_FULL), 64, r0, h, b);
+      const uint64_t pol = l2_policy_evict_first();
+      tma_load_4d_hint(sbase + kQOff, &tmQ, bar(Q_FULL), 0, r0, h, b, pol);
+      tma_load_4d_hint(sbase + kQOff + kQBytes / 2, &tmQ, bar(Q_FULL), 64, r0, h, b, pol);
     }
   }
   if (warp == 5) {
@@ -456,6 +460,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float inv = (l_run > 0.f) ? 1.0f / l_run : 0.0f;
       T* orow = static_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh + static_cast<long long>(r_abs) * p.o_sl;
       const bool row_ok = r_abs < p.L;
+      const uint64_t opol = l2_policy_evict_first();
 #pragma unroll 1
       for (int ch = 0; ch < 4; ++ch) {
         uint32_t ov[32];
@@ -474,7 +479,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4)
-            dst[q4] = make_uint4(pkd[4 * q4], pkd[4 * q4 + 1], pkd[4 * q4 + 2], pkd[4 * q4 + 3]);
+            st_global_v4_hint(dst + q4, make_uint4(pkd[4 * q4], pkd[4 * q4 + 1], pkd[4 * q4 + 2], pkd[4 * q4 + 3]),
+                              opol);
         }
       }
     }
