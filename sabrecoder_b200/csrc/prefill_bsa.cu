@@ -365,15 +365,37 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int tcount = trow ? min(p.cnt[b * p.cnt_sb + h * p.cnt_sh + ((r0 + half * 64) / 64) * p.cnt_sm],
                                   p.max_active) : 0;
     UnionIter it(bits, bits + kWords, nw);
+    // Token-level variant: a tile's mask word is loaded one tile ahead, so
+    // the load has a whole softmax step to arrive (it decides whether the
+    // warp skips the tile, before the S wait).
+    auto tok_load = [&](int kt2) -> unsigned long long {
+      const bool v2 = (bits[half * kWords + (kt2 >> 5)] >> (kt2 & 31)) & 1u;
+      const unsigned long long w2 = (v2 && rank < tcount) ? p.tmask[(tbase + rank) * 64 + (row & 63)] : 0ull;
+      rank += v2 ? 1 : 0;
+      return w2;
+    };
+    int kt_ahead = -1;
+    unsigned long long tw_ahead = 0ull;
+    if constexpr (kTok) {
+      if (n > 0) {
+        kt_ahead = it.next();
+        tw_ahead = tok_load(kt_ahead);
+      }
+    }
     for (int j = 0; ok && j < n; ++j) {
-      const int kt = it.next();
-      const bool vis = (bits[half * kWords + (kt >> 5)] >> (kt & 31)) & 1u;
+      int kt;
       unsigned long long tw = ~0ull;
       if constexpr (kTok) {
-        // issued before the S wait so the load overlaps it
-        tw = (vis && rank < tcount) ? p.tmask[(tbase + rank) * 64 + (row & 63)] : 0ull;
-        rank += vis ? 1 : 0;
+        kt = kt_ahead;
+        tw = tw_ahead;
+        if (j + 1 < n) {
+          kt_ahead = it.next();
+          tw_ahead = tok_load(kt_ahead);
+        }
+      } else {
+        kt = it.next();
       }
+      const bool vis = (bits[half * kWords + (kt >> 5)] >> (kt & 31)) & 1u;
       const int nvalid = vis ? min(64, max(0, r_abs - kt * 64 + 1)) : 0;
       // A warp whose 32 rows see no key of this tile (the tile is listed
       // only by the other half, lies wholly after the rows, or their token
