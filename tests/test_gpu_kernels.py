@@ -196,6 +196,34 @@ def test_prefill_config0_shape(K):
     assert K.device_status(clear=True) == 0
 
 
+@pytest.mark.parametrize("L", [65536, 65536 - 37])
+def test_prefill_at_the_maximum_length(K, L):
+    """The longest prompt the kernel takes (L <= 65536: 1024 key tiles, the
+    last bit of its key-tile bitmaps), also with a ragged last block; 8 query
+    / 4 KV heads, so K/V (134 MB) exceed L2 and the CTAs run head-major.
+    Lists shared by all heads (the reference's layout): the sink, a 4-block
+    window, the block at half the row and 6 random earlier blocks."""
+    block, Hq, Hkv, D = 64, 8, 4, 128
+    gen = torch.Generator().manual_seed(L)
+    q, k, v = (torch.randn(1, H, L, D, generator=gen).to(torch.bfloat16) for H in (Hq, Hkv, Hkv))
+    nb = (L + block - 1) // block
+    rng = np.random.default_rng(L)
+    m = np.zeros((1, nb, nb), dtype=bool)
+    for qb in range(nb):
+        m[0, qb, 0] = True
+        m[0, qb, max(0, qb - 3):qb + 1] = True
+        m[0, qb, qb // 2] = True
+        m[0, qb, rng.integers(0, qb + 1, size=6)] = True
+    idx, cnt = MO.block_indices_from_mask(m)
+    bi, bc = torch.from_numpy(idx), torch.from_numpy(cnt)
+    K.device_status(clear=True)
+    out = K.prefill_bsa(q.cuda(), k.cuda(), v.cuda(), bi.cuda(), bc.cuda(), block)
+    torch.cuda.synchronize()
+    assert K.device_status(clear=True) == 0
+    ref = AO.sparse_prefill_fp32_gathered(q, k, v, bi, bc, block)
+    _close(out, ref)
+
+
 def _kernel_mask(K, g):
     p = G.params(g)
     L = int(g["seq_len"])
@@ -298,7 +326,9 @@ def test_pooled_topk_bit_exact(K, B, Hq, Hkv, L, block, topk):
                                                          (2, 8, 2, 40, 64, False),
                                                          # blocks of three and four 64-row pieces: a split's
                                                          # share may start and end inside a block
-                                                         (2, 14, 2, 2500, 192, False), (1, 8, 1, 4000, 256, True)])
+                                                         (2, 14, 2, 2500, 192, False), (1, 8, 1, 4000, 256, True),
+                                                         # long caches: lists of ~800 blocks over up to 296 splits
+                                                         (1, 8, 1, 131072 + 33, 64, True), (1, 2, 2, 70000, 64, False)])
 def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
     gen = torch.Generator().manual_seed(Tmax + Hq)
     D = 128
