@@ -106,17 +106,27 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete. Gives up (returns
-// false) when *abort is set by another thread of the CTA or after kWaitNs; on
-// its own timeout it records SABRE_DEV_TIMEOUT and sets *abort.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+// false) when *abort is set by another thread of the CTA or after `lim`
+// nanoseconds (the device's wait limit, g_wait_limit_ns); on its own timeout
+// it records SABRE_DEV_TIMEOUT and sets *abort.
+// At the default limit a poll may suspend the thread (try_wait) and the
+// clock is read every 64 polls; kFastPolls suspending polls may come before
+// the clock is first read (measured per kernel whether they pay). Under a
+// shorter limit the polls never suspend (test_wait) and the clock is read
+// after each, so the limit holds to within a poll.
+template <int kFastPolls = 0>
+__device__ __forceinline__ bool mbar_wait_lim(uint32_t bar, uint32_t parity, volatile int* abort,
+                                              unsigned long long lim) {
   if (mbar_test_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  const unsigned long long lim = *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns);
-  // At the default limit a poll may suspend the thread (try_wait) and the
-  // clock is read every 64 polls. Under a shorter limit the polls never
-  // suspend (test_wait) and the clock is read after each, so the limit holds
-  // to within a poll.
   const bool short_limit = lim < kWaitNs;
+  if (!short_limit) {
+#pragma unroll 1
+    for (int i = 0; i < kFastPolls; ++i) {
+      if (mbar_try_wait(bar, parity)) return true;
+      if (*abort) return false;
+    }
+  }
+  const unsigned long long t0 = globaltimer_ns();
   const uint32_t every = short_limit ? 0u : 63u;
   for (uint32_t i = 0;; ++i) {
     if (short_limit ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
@@ -129,12 +139,34 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
-// Warp-level wait: lane 0 waits, the result is broadcast, and __syncwarp
+// The device's current wait limit (one global load; a kernel that waits
+// often reads it once and passes it to mbar_wait_lim).
+__device__ __forceinline__ unsigned long long wait_limit_ns() {
+  return *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+}
+
+// mbar_wait_lim with the limit read when a wait does not complete at once.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  if (mbar_test_wait(bar, parity)) return true;
+  return mbar_wait_lim(bar, parity, abort, wait_limit_ns());
+}
+
+// Warp-level waits: lane 0 waits, the result is broadcast, and __syncwarp
 // orders the other lanes after the observed phase. Keeps the warp converged
 // for the .sync.aligned tcgen05 instructions that follow.
 __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort) {
   bool ok = true;
   if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  __syncwarp();
+  return ok;
+}
+
+template <int kFastPolls = 0>
+__device__ __forceinline__ bool mbar_wait_warp_lim(uint32_t bar, uint32_t parity, volatile int* abort,
+                                                   unsigned long long lim) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait_lim<kFastPolls>(bar, parity, abort, lim);
   ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
   __syncwarp();
   return ok;
