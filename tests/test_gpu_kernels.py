@@ -196,18 +196,19 @@ def test_prefill_config0_shape(K):
     assert K.device_status(clear=True) == 0
 
 
-@pytest.mark.parametrize("L", [65536, 65536 - 37])
-def test_prefill_at_the_maximum_length(K, L):
+@pytest.mark.parametrize("L,block", [(65536, 64), (65536 - 37, 64), (65536 - 37, 128)])
+def test_prefill_at_the_maximum_length(K, L, block):
     """The longest prompt the kernel takes (L <= 65536: 1024 key tiles, the
-    last bit of its key-tile bitmaps), also with a ragged last block; 8 query
-    / 4 KV heads, so K/V (134 MB) exceed L2 and the CTAs run head-major.
-    Lists shared by all heads (the reference's layout): the sink, a 4-block
-    window, the block at half the row and 6 random earlier blocks."""
-    block, Hq, Hkv, D = 64, 8, 4, 128
-    gen = torch.Generator().manual_seed(L)
+    last bit of its key-tile bitmaps), also with a ragged last block and with
+    128-token blocks; 8 query / 4 KV heads, so K/V (134 MB) exceed L2 and the
+    CTAs run head-major. Lists shared by all heads (the reference's layout):
+    the sink, a 4-block window, the block at half the row and 6 random
+    earlier blocks."""
+    Hq, Hkv, D = 8, 4, 128
+    gen = torch.Generator().manual_seed(L + block)
     q, k, v = (torch.randn(1, H, L, D, generator=gen).to(torch.bfloat16) for H in (Hq, Hkv, Hkv))
     nb = (L + block - 1) // block
-    rng = np.random.default_rng(L)
+    rng = np.random.default_rng(L + block)
     m = np.zeros((1, nb, nb), dtype=bool)
     for qb in range(nb):
         m[0, qb, 0] = True
