@@ -8,6 +8,7 @@ last KV-head group) is checked against the oracle over every query row:
 
 * c1: deepseek-coder-1.3B attention, L=12288, 16 heads, block 64,
   structure lists + per-head pooled top-8;
+* c2: the same at a ragged prompt length (14001 tokens);
 * c3: 6.7B attention, L=16384, 32 heads, block 64, structure + top-8;
 * c4: 33B attention, L=16384, 56 query / 8 KV heads, block 128, structure
   lists only.
@@ -57,7 +58,7 @@ def _bench_lists(K, name, q, k, L):
     from sabrecoder_b200.spans import BENCH_SPAN_MIX, make_spans
     mask, topk = bench.mask_cfg(name)
     mix = bench.C4_SPAN_MIX if name == "c4" else BENCH_SPAN_MIX
-    seed = {"c1": 1000, "c3": 3000, "c4": 4000}[name]
+    seed = {"c1": 1000, "c2": 2000, "c3": 3000, "c4": 4000}[name]
     spans = make_spans(L, seed, **mix)
     mb = StructureAwareMaskBuilder(None, **mask)
     bi, bc, bm = mb.build_block_indices_from_spans(spans, torch.device("cuda"))
@@ -82,6 +83,8 @@ def _check(out, q, k, v, bi, bc, blk, heads):
 
 @pytest.mark.parametrize("name,Hq,Hkv,L,heads", [
     ("c1", 16, 16, 12288, [0, 7, 15]),
+    # one of config 2's prompt lengths (12288-16384), not a multiple of 64 or 128
+    ("c2", 16, 16, 14001, [0, 15]),
     ("c3", 32, 32, 16384, [0, 31]),
     ("c4", 56, 8, 16384, [0, 6, 49, 55]),
 ])
