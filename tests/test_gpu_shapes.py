@@ -14,7 +14,9 @@ last KV-head group) is checked against the oracle over every query row:
   lists only.
 
 Tolerance (bf16): max-abs 2e-2, mean-abs 2e-3. The per-head top-8 lists are
-also compared with the oracle's (bit-exact) at the c1 shape.
+also compared with the oracle's (bit-exact) at the c1 shape, and the
+token-level variant runs on the c1 prompt against the oracle's dense token
+mask (lists bit-exact, two heads over every row).
 """
 
 import numpy as np
@@ -117,3 +119,53 @@ def test_c1_topk_lists_match_oracle(K):
         for r in range(ext.shape[-2]):
             c = int(cnt[0, h, r])
             np.testing.assert_array_equal(got[0, h, r, :c], idx[0, h, r, :c])
+
+
+def test_token_mode_at_the_c1_prompt(K):
+    """The token-level variant (use_token_level_sparsity; the reference's
+    _fwd_kernel_sabrecoder_token_sparse, sabrecoder_attention_triton.py:119-215)
+    on the c1 prompt: 12288 tokens with the benchmark's structure spans, the
+    block lists and per-pair 64x64 masks built on the GPU from the token rule.
+    The lists equal the blocks of the oracle's dense token mask, and two heads
+    match the oracle's token-masked attention over every query row."""
+    from sabrecoder_b200.spans import BENCH_SPAN_MIX, make_spans
+    L, H, blk = 12288, 2, 64
+    spans = make_spans(L, 1000, **BENCH_SPAN_MIX)
+    t2c, grp, glob, dep, n = bench._token_rule_from_spans(spans, bench.MASK)
+    dev = torch.device("cuda")
+
+    def up(a, dt):
+        return torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(dev)
+
+    tc, tg, tgl = up(t2c, torch.int32), up(grp, torch.int32), up(glob, torch.uint8)
+    db = up(dep.view(np.int32), torch.int32)
+    w = bench.MASK["window_size"]
+    bits = K.token_block_mask(tc, tg, tgl, db, n, w)
+    nb = bits.shape[0]
+    idx, cnt, mx = K.indices_from_bits(bits, nb)
+    lists = idx[:, :max(int(mx.item()), 1)].contiguous()
+    masks = K.token_tile_masks(tc, tg, tgl, db, n, w, lists, cnt)
+    q, k, v = _qkv(H, H, L, seed=11)
+    out = K.prefill_bsa(q, k, v, lists[None], cnt[None], blk, token_masks=masks)
+    torch.cuda.synchronize()
+    assert K.device_status(clear=True) == 0
+
+    vis = MO.token_level_mask_tokens(spans.token_to_chunk(), len(spans.spans), spans.import_chunks, spans.deps,
+                                     spans.signature_token_mask(), seq_len=L, **bench.MASK)
+    ref_idx, ref_cnt = MO.block_indices_from_mask(MO.block_mask_from_token_mask(vis, blk))
+    np.testing.assert_array_equal(cnt.cpu().numpy(), ref_cnt)
+    got_lists = lists.cpu().numpy()
+    for r in range(nb):
+        c = int(ref_cnt[r])
+        np.testing.assert_array_equal(got_lists[r, :c], ref_idx[r, :c])
+
+    qc, kc, vc, got = q.cpu(), k.cpu(), v.cpu(), out.float().cpu()
+    dmax, dsum = 0.0, 0.0
+    for r0 in range(0, L, 2048):
+        r1 = min(L, r0 + 2048)
+        ref = AO.token_masked_prefill_fp32(qc[:, :, r0:r1], kc[:, :, :r1], vc[:, :, :r1],
+                                           torch.from_numpy(vis[r0:r1, :r1]))
+        d = (got[:, :, r0:r1] - ref).abs()
+        dmax, dsum = max(dmax, d.max().item()), dsum + d.sum().item()
+    assert dmax <= MAX_ABS, f"max-abs {dmax:.3e}"
+    assert dsum / got.numel() <= MEAN_ABS, f"mean-abs {dsum / got.numel():.3e}"
