@@ -16,7 +16,9 @@ last KV-head group) is checked against the oracle over every query row:
 Tolerance (bf16): max-abs 2e-2, mean-abs 2e-3. The per-head top-8 lists are
 also compared with the oracle's (bit-exact) at the c1 shape, and the
 token-level variant runs on the c1 prompt against the oracle's dense token
-mask (lists bit-exact, two heads over every row).
+mask (lists bit-exact, two heads over every row). Decode attention runs at
+the decode-op benchmark's c1 / c3 / c4 shapes, dense and sparse lists, from a
+CUDA graph as the benchmark times it.
 """
 
 import numpy as np
@@ -169,3 +171,66 @@ def test_token_mode_at_the_c1_prompt(K):
         dmax, dsum = max(dmax, d.max().item()), dsum + d.sum().item()
     assert dmax <= MAX_ABS, f"max-abs {dmax:.3e}"
     assert dsum / got.numel() <= MEAN_ABS, f"mean-abs {dsum / got.numel():.3e}"
+
+
+@pytest.mark.parametrize("name", ["c1", "c3", "c4"])
+@pytest.mark.parametrize("lists", ["dense", "sparse"])
+def test_decode_at_benched_shape(K, name, lists):
+    """Decode attention at the shapes the decode-op benchmark reports (c1:
+    16 heads, 12288 + 64 cached tokens; c3: 32 heads, 16384 + 128; c4: 56
+    query / 8 KV heads, block 128, 16384 + 64), dense lists (the reference
+    decodes densely, sabrecoder_llama_triton.py:254-268) and the sparse lists
+    the benchmark builds (the last prompt row's structure list plus every
+    generated block). As the benchmark times it, the calls run from one CUDA
+    graph over two layer caches (the split kernels are programmatic dependent
+    launches); both outputs are checked against the oracle."""
+    from sabrecoder_b200.sabrecoder_attention import StructureAwareMaskBuilder
+    from sabrecoder_b200.spans import BENCH_SPAN_MIX, make_spans
+    Hq, H, L, gen = bench.DECODE_SHAPES[name]
+    mask, _ = bench.mask_cfg(name)
+    blk = mask["block_size"]
+    T = L + gen
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(21)
+    caches = [tuple(torch.randn(1, H, T, 128, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(2))
+              for _ in range(2)]
+    q = torch.randn(1, Hq, 128, device=dev, generator=g, dtype=torch.bfloat16)
+    nbk = (T + blk - 1) // blk
+    if lists == "dense":
+        lst = torch.arange(nbk, device=dev, dtype=torch.int32).unsqueeze(0)
+    else:
+        mb = StructureAwareMaskBuilder(None, **mask)
+        mix = bench.C4_SPAN_MIX if name == "c4" else BENCH_SPAN_MIX
+        bi, bc, _ = mb.build_block_indices_from_spans(make_spans(L, 1000, **mix), dev)
+        nb_p = (L + blk - 1) // blk
+        c_last = int(bc[0, nb_p - 1].item())
+        lst = torch.cat([bi[0, nb_p - 1, :c_last].to(torch.int32),
+                         torch.arange(nb_p, nbk, device=dev, dtype=torch.int32)]).unsqueeze(0).contiguous()
+    cnt = torch.tensor([lst.shape[1]], dtype=torch.int32, device=dev)
+    seq = torch.tensor([T], dtype=torch.int32, device=dev)
+    ws = torch.empty(K.decode_workspace_bytes(1, Hq, H, 128, lst.shape[1]), dtype=torch.uint8, device=dev)
+    outs = [torch.empty_like(q) for _ in caches]
+
+    def step():
+        for (kc, vc), o in zip(caches, outs):
+            K.decode_bsa(q, kc, vc, lst, cnt, seq, blk, out=o, workspace=ws)
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    for o in outs:
+        o.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert K.device_status(clear=True) == 0
+    for (kc, vc), o in zip(caches, outs):
+        ref = AO.sparse_decode_fp32(q.cpu(), kc.cpu(), vc.cpu(), lst.cpu(), cnt.cpu(), seq.cpu(), blk)
+        d = (o.float().cpu() - ref).abs()
+        assert d.max().item() <= MAX_ABS and d.mean().item() <= MEAN_ABS, (d.max().item(), d.mean().item())
+    del graph
