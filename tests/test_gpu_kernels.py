@@ -544,11 +544,18 @@ def test_qkv_proj_rope_matches_projection_and_hf_rope(K, B, L, hidden, Hq, Hkv, 
     assert K.device_status(clear=True) == 0
 
 
-def test_qkv_proj_rope_at_the_1p3b_layer_shape(K):
-    """One c1 layer: 12288 tokens, hidden 2048, 16 + 16 + 16 heads, pooled by 64."""
+@pytest.mark.parametrize("L,hidden,Hq,Hkv,pool", [
+    (12288, 2048, 16, 16, 64),    # c1: deepseek-coder-1.3B layer
+    (16384, 4096, 32, 32, 64),    # c3: 6.7B layer
+    (16384, 7168, 56, 8, 128),    # c4: 33B layer (GQA 7:1), pooled by 128
+])
+def test_qkv_proj_rope_at_the_benched_layer_shapes(K, L, hidden, Hq, Hkv, pool):
+    """One layer of each benched model: projection within bf16 rounding of
+    cuBLAS, q/k bit-exact with apply_rotary_pos_emb of the kernel's own
+    projection, v and the pooled means exact."""
     from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
     gen = torch.Generator(device="cuda").manual_seed(3)
-    B, L, hidden, Hq, Hkv, D = 1, 12288, 2048, 16, 16, 128
+    B, D = 1, 128
     N = (Hq + 2 * Hkv) * D
     x = (torch.randn(B, L, hidden, generator=gen, device="cuda") * 0.5).to(torch.bfloat16)
     w = (torch.randn(N, hidden, generator=gen, device="cuda") / hidden ** 0.5).to(torch.bfloat16)
@@ -559,7 +566,7 @@ def test_qkv_proj_rope_at_the_1p3b_layer_shape(K):
     vc = torch.zeros_like(kc)
     q_out = torch.empty(B, L, Hq, D, dtype=torch.bfloat16, device="cuda")
     y = torch.empty(B * L, N, dtype=torch.bfloat16, device="cuda")
-    qp, kp = K.qkv_proj_rope(x, w, cos, sin, q_out, kc, vc, pool_block=64, y_out=y)
+    qp, kp = K.qkv_proj_rope(x, w, cos, sin, q_out, kc, vc, pool_block=pool, y_out=y)
     ref = torch.nn.functional.linear(x, w).view(B * L, N)  # cuBLAS, bf16 out
     torch.cuda.synchronize()
     d = (y.float() - ref.float()).abs()
@@ -571,5 +578,7 @@ def test_qkv_proj_rope_at_the_1p3b_layer_shape(K):
     assert torch.equal(vc[:, :, :L], yv[:, :, Hq + Hkv:].transpose(1, 2))
     for h in (0, Hq - 1):
         np.testing.assert_array_equal(qp[:, h:h + 1].cpu().numpy(),
-                                      MO.pooled_block_means(rq[:, h:h + 1].float().cpu().numpy(), L, 64))
+                                      MO.pooled_block_means(rq[:, h:h + 1].float().cpu().numpy(), L, pool))
+    np.testing.assert_array_equal(kp[:, Hkv - 1:].cpu().numpy(),
+                                  MO.pooled_block_means(rk[:, Hkv - 1:].float().cpu().numpy(), L, pool))
     assert K.device_status(clear=True) == 0
