@@ -401,7 +401,9 @@ def test_decode_strided_cache_vs_oracle(K, block, row_pad, Hq):
 
 
 @pytest.mark.parametrize("B,hidden,Hq,Hkv,dtype", [(1, 2048, 16, 16, torch.bfloat16), (3, 1024, 8, 2, torch.bfloat16),
-                                                  (2, 1792, 14, 2, torch.float16)])
+                                                  (2, 1792, 14, 2, torch.float16),
+                                                  # the 6.7B and 33B decode-step shapes
+                                                  (1, 4096, 32, 32, torch.bfloat16), (1, 7168, 56, 8, torch.bfloat16)])
 def test_qkv_rope_decode_vs_unfused(K, B, hidden, Hq, Hkv, dtype):
     """The fused decode projection + rotary + KV store against the unfused
     computation (cuBLAS projection rounded to the dtype, then transformers'
