@@ -466,7 +466,10 @@ def test_rope_qkv_batch_with_one_shared_table(K):
 
 
 @pytest.mark.parametrize("B,L,Hq,Hkv,pool,dtype", [(1, 1000, 4, 2, 64, torch.bfloat16), (2, 300, 2, 2, 128, torch.bfloat16),
-                                                   (1, 1, 4, 4, 0, torch.bfloat16), (1, 257, 2, 1, 64, torch.float16)])
+                                                   (1, 1, 4, 4, 0, torch.bfloat16), (1, 257, 2, 1, 64, torch.float16),
+                                                   # the c1 and c4 layer shapes of the benchmark
+                                                   (1, 12288, 16, 16, 64, torch.bfloat16),
+                                                   (1, 16384, 56, 8, 128, torch.bfloat16)])
 def test_rope_qkv_bit_exact_with_hf(K, B, L, Hq, Hkv, pool, dtype):
     """Fused RoPE + KV store equals transformers' apply_rotary_pos_emb bit for
     bit; pools equal the oracle's block means of the rotated rows."""
