@@ -14,7 +14,7 @@ last KV-head group) is checked against the oracle over every query row:
   lists only.
 
 Tolerance (bf16): max-abs 2e-2, mean-abs 2e-3. The per-head top-8 lists are
-also compared with the oracle's (bit-exact) at the c1 shape, and the
+also compared with the oracle's (bit-exact) at the c1 and c3 shapes, and the
 token-level variant runs on the c1 prompt against the oracle's dense token
 mask (lists bit-exact, two heads over every row). Decode attention runs at
 the decode-op benchmark's c1 / c3 / c4 shapes, dense and sparse lists, from a
@@ -105,19 +105,20 @@ def test_prefill_at_benched_shape(K, name, Hq, Hkv, L, heads):
     print(f"{name}: L={L} Hq={Hq} Hkv={Hkv} block {blk} density {dens:.4f} max_active {bi.shape[-1]}")
 
 
-def test_c1_topk_lists_match_oracle(K):
-    """The per-head pooled top-8 lists of the c1 shape equal the oracle's
-    (pooled fp32 block means, fixed-order scores, ties to the lower block)."""
-    L = 12288
-    q, k, v = _qkv(16, 16, L, seed=7)
-    bi, bc, bm, blk, topk = _bench_lists(K, "c1", q, k, L)
+@pytest.mark.parametrize("name,H,L", [("c1", 16, 12288), ("c3", 32, 16384)])
+def test_topk_lists_match_oracle(K, name, H, L):
+    """The per-head pooled top-8 lists of the c1 and c3 shapes equal the
+    oracle's (pooled fp32 block means, fixed-order scores, ties to the lower
+    block)."""
+    q, k, v = _qkv(H, H, L, seed=7)
+    bi, bc, bm, blk, topk = _bench_lists(K, name, q, k, L)
     qm = MO.pooled_block_means(q.float().cpu().numpy(), L, blk)
     km = MO.pooled_block_means(k.float().cpu().numpy(), L, blk)
     ext = MO.topk_extend_mask(bm.cpu().numpy().astype(bool), MO.pooled_scores(qm, km), topk)
     idx, cnt = MO.block_indices_from_mask(ext)
     np.testing.assert_array_equal(bc.cpu().numpy(), cnt)
     got = bi.cpu().numpy()
-    for h in range(16):
+    for h in range(H):
         for r in range(ext.shape[-2]):
             c = int(cnt[0, h, r])
             np.testing.assert_array_equal(got[0, h, r, :c], idx[0, h, r, :c])
