@@ -20,6 +20,14 @@ constexpr int kRowsPerHalf = 4;     // rows per half-warp per step
 constexpr int kRowsPerStep = 4 * 2 * kRowsPerHalf;  // 32 rows per CTA step
 constexpr int kTargetCtas = 2 * 148;
 constexpr int kMaxSplits = 256;
+// Merge kernel: for more than kCombineWide splits per query head, four groups
+// of kD threads each take every fourth split with 16 loads in flight per
+// thread (one round of loads); fewer splits are merged by one group of kD
+// threads, 8 loads at a time (measured faster there).
+constexpr int kCombineWide = 16;
+constexpr int kCombineGroups = 4;
+static inline bool combine_wide(int splits) { return splits > kCombineWide; }
+static inline int combine_threads(int splits) { return combine_wide(splits) ? kD * kCombineGroups : kD; }
 
 struct Params {
   const void* q;
@@ -526,51 +534,78 @@ __global__ void __launch_bounds__(kBulkThreads, 2) decode_bulk_kernel(const Para
   }
 }
 
-// One CTA per (b, query head): merge the splits in index order. Launched as
-// a programmatic dependent of the split kernel: it may start while the split
-// kernel's last CTAs run, and waits here until that grid has finished and its
-// partials are visible.
-// The (m, l) of all splits are read in one parallel pass into shared memory
-// and each thread's acc values in independent groups of 8, so the loads do
-// not wait on one another; the sums run in split order as before.
-template <typename T>
-__global__ void __launch_bounds__(kD) decode_combine_kernel(const Params p) {
+// One CTA per (b, query head): merge the splits. Launched as a programmatic
+// dependent of the split kernel: it may start while the split kernel's last
+// CTAs run, and waits here until that grid has finished and its partials are
+// visible.
+// The (m, l) of all splits are read in one parallel pass into shared memory;
+// each of kGroups thread groups then sums every kGroups-th split's acc
+// values with kBatch loads issued together (with 4 groups of 16, one round
+// trip for up to 64 splits), and the group sums are added in group order, so
+// the result is deterministic.
+template <typename T, int kGroups, int kBatch>
+__global__ void __launch_bounds__(kD * kGroups) decode_combine_kernel(const Params p) {
   // The next decode call's split kernel (a programmatic dependent too) may
   // start its set-up now; it waits for this grid before touching memory.
   if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float sm_m[kMaxSplits], sm_l[kMaxSplits];
+  __shared__ float sm_L[kGroups][kD], sm_A[kGroups][kD];
   const int bh = blockIdx.x;
   const int b = bh / p.Hq;
   const int h = bh - b * p.Hq;
-  const int d = threadIdx.x;
+  const int d = threadIdx.x % kD;
+  const int grp = threadIdx.x / kD;
   const long long base = static_cast<long long>(bh) * p.splits;
-  for (int s = d; s < p.splits; s += kD) {
+  for (int s = threadIdx.x; s < p.splits; s += kD * kGroups) {
     sm_m[s] = p.part_ml[(base + s) * 2];
     sm_l[s] = p.part_ml[(base + s) * 2 + 1];
   }
   __syncthreads();
   float M = -INFINITY;
   for (int s = 0; s < p.splits; ++s) M = fmaxf(M, sm_m[s]);
+  // Thread group g takes splits g, g + G, g + 2G, ... with kBatch loads in
+  // flight.
   float L = 0.f, A = 0.f;
   if (M != -INFINITY) {
-    for (int s0 = 0; s0 < p.splits; s0 += 8) {
-      float a[8];
+    for (int s0 = grp; s0 < p.splits; s0 += kGroups * kBatch) {
+      float a[kBatch];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) a[u] = (s0 + u < p.splits) ? p.part_acc[(base + s0 + u) * kD + d] : 0.f;
+      for (int u = 0; u < kBatch; ++u) {
+        const int s = s0 + u * kGroups;
+        a[u] = (s < p.splits) ? p.part_acc[(base + s) * kD + d] : 0.f;
+      }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (s0 + u < p.splits) {
-          const float w = ex2(sm_m[s0 + u] - M);
-          L += w * sm_l[s0 + u];
+      for (int u = 0; u < kBatch; ++u) {
+        const int s = s0 + u * kGroups;
+        if (s < p.splits) {
+          const float w = ex2(sm_m[s] - M);
+          L += w * sm_l[s];
           A += w * a[u];
         }
       }
     }
   }
-  const float out = (L > 0.f) ? A / L : 0.f;
-  T* op = static_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh;
-  op[d] = DT<T>::from_f(out);
+  if constexpr (kGroups == 1) {
+    const float out = (L > 0.f) ? A / L : 0.f;
+    T* op = static_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh;
+    op[d] = DT<T>::from_f(out);
+    return;
+  }
+  sm_L[grp][d] = L;
+  sm_A[grp][d] = A;
+  __syncthreads();
+  if (grp == 0) {
+    float Lt = 0.f, At = 0.f;
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) {  // fixed order: deterministic
+      Lt += sm_L[g][d];
+      At += sm_A[g][d];
+    }
+    const float out = (Lt > 0.f) ? At / Lt : 0.f;
+    T* op = static_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh;
+    op[d] = DT<T>::from_f(out);
+  }
 }
 
 template <typename T, int G>
@@ -630,7 +665,7 @@ static cudaError_t launch_decode(const Params& p, int g, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.B * p.Hq);
-  cfg.blockDim = dim3(kD);
+  cfg.blockDim = dim3(combine_threads(p.splits));
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -638,7 +673,8 @@ static cudaError_t launch_decode(const Params& p, int g, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_combine_kernel<T>, p);
+  return combine_wide(p.splits) ? cudaLaunchKernelEx(&cfg, decode_combine_kernel<T, kCombineGroups, 16>, p)
+                                : cudaLaunchKernelEx(&cfg, decode_combine_kernel<T, 1, 8>, p);
 }
 
 }  // namespace decode

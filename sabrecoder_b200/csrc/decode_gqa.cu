@@ -387,7 +387,7 @@ static int decode_gqa_launch(const Params& p, int dtype, cudaStream_t s) {
   dim3 grid(p.splits, p.Hkv, p.B);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.B * p.Hq);
-  cfg.blockDim = dim3(kD);
+  cfg.blockDim = dim3(combine_threads(p.splits));
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -399,12 +399,16 @@ static int decode_gqa_launch(const Params& p, int dtype, cudaStream_t s) {
     if ((st = ensure_smem_attr(gqa::decode_gqa_kernel<__nv_bfloat16>, gqa::kSmemBytes)) != SABRE_OK) return st;
     SABRE_CUDA_TRY(launch_pdl(grid, gqa::kThreads, gqa::kSmemBytes, s, gqa::decode_gqa_kernel<__nv_bfloat16>, mk, mv, p));
     SABRE_CUDA_TRY(cudaGetLastError());
-    SABRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_combine_kernel<__nv_bfloat16>, p));
+    SABRE_CUDA_TRY(combine_wide(p.splits)
+                       ? cudaLaunchKernelEx(&cfg, decode_combine_kernel<__nv_bfloat16, kCombineGroups, 16>, p)
+                       : cudaLaunchKernelEx(&cfg, decode_combine_kernel<__nv_bfloat16, 1, 8>, p));
   } else {
     if ((st = ensure_smem_attr(gqa::decode_gqa_kernel<__half>, gqa::kSmemBytes)) != SABRE_OK) return st;
     SABRE_CUDA_TRY(launch_pdl(grid, gqa::kThreads, gqa::kSmemBytes, s, gqa::decode_gqa_kernel<__half>, mk, mv, p));
     SABRE_CUDA_TRY(cudaGetLastError());
-    SABRE_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_combine_kernel<__half>, p));
+    SABRE_CUDA_TRY(combine_wide(p.splits)
+                       ? cudaLaunchKernelEx(&cfg, decode_combine_kernel<__half, kCombineGroups, 16>, p)
+                       : cudaLaunchKernelEx(&cfg, decode_combine_kernel<__half, 1, 8>, p));
   }
   return SABRE_OK;
 }
