@@ -101,7 +101,9 @@ int sabre_prefill_bsa(const void* q, const void* k, const void* v, void* o, cons
  * block_indices : int32 [B, Hidx, max_active] strides {b, h, k} (h-stride 0
  *             = shared), block_counts int32 [B, Hidx] strides {b, h}
  * seq_lens  : int32 [B] device: keys t >= seq_lens[b] are masked
- * workspace : >= sabre_decode_workspace_size(...) bytes of device memory
+ * workspace : >= sabre_decode_workspace_size(...) bytes of device memory,
+ *             4-byte aligned (16-byte aligned lets the partials be stored 16
+ *             bytes at a time)
  * ---------------------------------------------------------------------- */
 size_t sabre_decode_workspace_size(int batch, int heads_q, int heads_kv, int head_dim, int max_active);
 int sabre_decode_bsa(const void* q, const void* k_cache, const void* v_cache, void* o,

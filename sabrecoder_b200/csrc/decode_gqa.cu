@@ -336,10 +336,17 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int c = 0; c < 32; ++c) ov[c] = 0u;
         }
         if (real) {
-          // 4-byte stores: the caller's workspace need only be float-aligned.
+          // 16-byte stores when the caller's workspace allows them (it need
+          // only be float-aligned), else 4-byte stores.
           float* dst = p.part_acc + slot * kD + ch * 32;
+          if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0u) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) dst[c] = __uint_as_float(ov[c]);
+            for (int c = 0; c < 32; c += 4)
+              *reinterpret_cast<uint4*>(dst + c) = make_uint4(ov[c], ov[c + 1], ov[c + 2], ov[c + 3]);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) dst[c] = __uint_as_float(ov[c]);
+          }
         }
       }
       if (real) {

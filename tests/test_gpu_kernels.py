@@ -353,6 +353,28 @@ def test_decode_vs_oracle(K, B, Hq, Hkv, Tmax, block, shared):
 
 
 @pytest.mark.parametrize("Hq,Hkv", [(4, 4), (8, 2)])
+def test_decode_with_a_workspace_only_float_aligned(K, Hq, Hkv):
+    """A workspace that is 4- but not 16-byte aligned (the split partials are
+    then stored 4 bytes at a time) gives the oracle's result, for the
+    CUDA-core and the tensor-core decode."""
+    gen = torch.Generator().manual_seed(Hq + 100)
+    B, T, D, block = 1, 3000, 128, 64
+    q = torch.randn(B, Hq, D, generator=gen).to(torch.bfloat16)
+    kc = torch.randn(B, Hkv, T, D, generator=gen).to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, T, D, generator=gen).to(torch.bfloat16)
+    nbk = (T + block - 1) // block
+    bi = torch.arange(nbk, dtype=torch.int32).unsqueeze(0)
+    bc = torch.tensor([nbk], dtype=torch.int32)
+    seq = torch.tensor([T], dtype=torch.int32)
+    need = K.decode_workspace_bytes(B, Hq, Hkv, D, nbk)
+    ws = torch.empty(need + 16, dtype=torch.uint8, device="cuda")[4:]
+    assert ws.data_ptr() % 16 == 4
+    out = K.decode_bsa(q.cuda(), kc.cuda(), vc.cuda(), bi.cuda(), bc.cuda(), seq.cuda(), block, workspace=ws)
+    torch.cuda.synchronize()
+    _close(out, AO.sparse_decode_fp32(q, kc, vc, bi, bc, seq, block))
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(4, 4), (8, 2)])
 def test_decode_f16_vs_oracle(K, Hq, Hkv):
     """fp16 caches: one query head per KV head (CUDA-core kernel) and four
     (tensor-core kernel)."""
