@@ -557,6 +557,14 @@ __global__ void __launch_bounds__(kD * kGroups) decode_combine_kernel(const Para
   const int d = threadIdx.x % kD;
   const int grp = threadIdx.x / kD;
   const long long base = static_cast<long long>(bh) * p.splits;
+  // Thread group g takes splits g, g + G, g + 2G, ... with kBatch loads in
+  // flight; the first batch is requested together with the (m, l) pass.
+  float a[kBatch];
+#pragma unroll
+  for (int u = 0; u < kBatch; ++u) {
+    const int s = grp + u * kGroups;
+    a[u] = (s < p.splits) ? p.part_acc[(base + s) * kD + d] : 0.f;
+  }
   for (int s = threadIdx.x; s < p.splits; s += kD * kGroups) {
     sm_m[s] = p.part_ml[(base + s) * 2];
     sm_l[s] = p.part_ml[(base + s) * 2 + 1];
@@ -564,16 +572,15 @@ __global__ void __launch_bounds__(kD * kGroups) decode_combine_kernel(const Para
   __syncthreads();
   float M = -INFINITY;
   for (int s = 0; s < p.splits; ++s) M = fmaxf(M, sm_m[s]);
-  // Thread group g takes splits g, g + G, g + 2G, ... with kBatch loads in
-  // flight.
   float L = 0.f, A = 0.f;
   if (M != -INFINITY) {
     for (int s0 = grp; s0 < p.splits; s0 += kGroups * kBatch) {
-      float a[kBatch];
+      if (s0 != grp) {
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int s = s0 + u * kGroups;
-        a[u] = (s < p.splits) ? p.part_acc[(base + s) * kD + d] : 0.f;
+        for (int u = 0; u < kBatch; ++u) {
+          const int s = s0 + u * kGroups;
+          a[u] = (s < p.splits) ? p.part_acc[(base + s) * kD + d] : 0.f;
+        }
       }
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
